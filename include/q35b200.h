@@ -1,0 +1,231 @@
+/*
+ * q35b200.h - C ABI of the B200 (sm_100a) Qwen3-VL-MoE decoder-layer kernels.
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream, enqueues
+ * its work on that stream and returns an int status (0 = success, see
+ * q35_status).  Nothing in this header depends on torch: any host language that
+ * can pass pointers (ctypes, cgo, JNI, N-API) can bind it.
+ *
+ * Conventions
+ *   - "bf16" buffers are IEEE bfloat16 stored as uint16; fp32 buffers are float.
+ *   - All buffers are dense row-major (C-contiguous) unless a stride is given.
+ *   - Pointers used with TMA (GEMM and attention operands) must be 16-byte
+ *     aligned and their row pitch a multiple of 16 bytes; violations return
+ *     Q35_ERR_ALIGN before anything is launched.
+ *   - A device-side failure (a bounded wait that ran out, an index out of range)
+ *     never traps: the kernel records it in a per-device error word and returns.
+ *     q35_device_error_check() synchronises the device and reports that word.
+ *
+ * Each declaration names the reference interface it replaces, as
+ * file:line within luozoupi/Qwen3_5_VL_CUDA_CUSTOM (paths relative to
+ * CUDA_qwen3_5-main/, REF below).
+ */
+#ifndef Q35B200_H
+#define Q35B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define Q35_API __attribute__((visibility("default")))
+#else
+#define Q35_API
+#endif
+
+typedef struct CUstream_st *q35_stream_t;
+
+enum q35_status {
+  Q35_OK = 0,
+  Q35_ERR_INVALID = 1,     /* null pointer, negative size, bad enum */
+  Q35_ERR_SHAPE = 2,       /* shape outside what the kernel supports */
+  Q35_ERR_ALIGN = 3,       /* pointer or pitch not 16-byte aligned */
+  Q35_ERR_UNSUPPORTED = 4, /* dtype / head_dim / feature not built */
+  Q35_ERR_CUDA = 5,        /* a CUDA runtime/driver call failed */
+  Q35_ERR_DEVICE = 6,      /* the device error word is set */
+  Q35_ERR_NO_DEVICE = 7    /* no sm_100 device is current */
+};
+
+/* ---- status / diagnostics (no reference counterpart: the reference raises
+ *      c10::Error through TORCH_CHECK, REF cuda_qwen3_vl/csrc/common.h:10-12) */
+Q35_API const char *q35_status_string(int status);
+/* Human-readable detail of the last non-zero status returned on this host thread. */
+Q35_API const char *q35_last_error_message(void);
+/* Synchronises the current device, copies its error word to info[0..3]
+ * (code, site, a, b), clears it and returns Q35_OK or Q35_ERR_DEVICE. */
+Q35_API int q35_device_error_check(int32_t *info4);
+/* Library build identity, e.g. "q35b200 sm_100a". */
+Q35_API const char *q35_version(void);
+
+/* ---- RMSNorm ------------------------------------------------------------
+ * y[r,:] = bf16( x[r,:] * rsqrt(mean(x[r,:]^2) + eps) * w ), fp32 inside.
+ * Replaces rmsnorm_forward(Tensor x, Tensor weight, float eps)
+ *   REF cuda_qwen3_vl/csrc/rmsnorm_op.cpp:9-12, kernel csrc/rmsnorm_op.cu:8-60.
+ * x, y: bf16 [rows, cols]; w: bf16 [cols].  cols % 8 == 0.                   */
+Q35_API int q35_rmsnorm_fwd(const void *x, const void *w, void *y, int64_t rows,
+                    int64_t cols, float eps, q35_stream_t stream);
+
+/* ---- QK-norm + mRoPE + head-major split ---------------------------------
+ * Input qkv: bf16 [B*S, (Hq + 2*Hkv) * D], the fused q/k/v projection output
+ * (token-major; columns q heads, then k heads, then v heads).
+ * Outputs (head-major): q [B,Hq,S,D], k [B,Hkv,S,D], v [B,Hkv,S,D] (bf16).
+ * q and k are RMS-normalised over D with qw/kw (bf16 [D]), then rotated with
+ * rotate-half RoPE whose angle for rotary index j is
+ *     pos[axis(j), b, s] * inv_freq[j mod D/2]      (fp32),
+ * axis(j) from the chunked mRoPE section layout (interleaved = 0) or the
+ * HF-interleaved T/H/W layout (interleaved = 1).  positions: int64 [3,B,S].
+ * Replaces the q_norm/k_norm + TextMRoPE.apply + mrope_forward chain
+ *   REF cuda_qwen3_vl/modules/attention.py:82-87, modules/rotary.py:46-59,
+ *   kernels/mrope.py:19-50,80-104, csrc/mrope_op.cpp:5-7.
+ * D must be 32, 64 or 128; sections is a HOST array of 3 ints summing to D/2;
+ * positions and inv_freq (fp32 [D/2]) are device arrays.                   */
+Q35_API int q35_qknorm_mrope_fwd(const void *qkv, const void *qw, const void *kw,
+                         const int64_t *positions, const float *inv_freq,
+                         const int32_t *sections, int interleaved, void *q,
+                         void *k, void *v, int64_t B, int64_t S, int Hq,
+                         int Hkv, int D, float eps, q35_stream_t stream);
+
+/* Apply mRoPE to a head-major tensor x [B,H,S,D] in place of
+ * mrope_forward(x, cos, sin) (REF csrc/mrope_op.cpp:5-7), computing cos/sin
+ * from positions like q35_qknorm_mrope_fwd (no normalisation).             */
+Q35_API int q35_mrope_fwd(const void *x, void *y, const int64_t *positions,
+                  const float *inv_freq, const int32_t *sections,
+                  int interleaved, int64_t B, int H, int64_t S, int D,
+                  q35_stream_t stream);
+
+/* ---- Router --------------------------------------------------------------
+ * logits[t,e] = sum_h x[t,h] * wg[e,h] (+ bias[e])  in fp32 (x bf16, wg fp32),
+ * p = softmax(logits[t,:]); idx[t,0..k) = top-k of p, sorted descending,
+ * ties to the lower expert index; weights[t,j] = p[idx] / sum_j p[idx]
+ * (renorm != 0) or p[idx] (renorm == 0).
+ * Replaces the router of CudaSparseMoE.forward (REF modules/moe.py:60-65):
+ *   matmul_forward (csrc/matmul_op.cpp:11-14) -> softmax_forward
+ *   (csrc/softmax_op.cpp:6-9) -> topk_forward (csrc/moe_routing_op.cpp:9-13).
+ * bias may be NULL.  E <= 256, k <= 16, H % 8 == 0.
+ * idx is int32 (the reference returns int64; values are equal).            */
+Q35_API int q35_router_topk_fwd(const void *x, const float *wg, const float *bias,
+                        float *logits, int32_t *idx, float *weights,
+                        int64_t T, int H, int E, int k, int renorm,
+                        q35_stream_t stream);
+
+/* Row softmax in fp32, replaces softmax_forward (REF csrc/softmax_op.cpp:6-9).
+ * x, y: fp32 [rows, cols], cols <= 4096.                                     */
+Q35_API int q35_softmax_fwd(const float *x, float *y, int64_t rows, int cols,
+                    q35_stream_t stream);
+
+/* Row top-k of fp32 values, sorted descending, ties to the lower column;
+ * replaces topk_forward (REF csrc/moe_routing_op.cpp:9-13, kernel
+ * csrc/moe_routing_op.cu:11-63).  vals fp32 [rows,k], idx int64 [rows,k].
+ * cols <= 4096, k <= 16.                                                    */
+Q35_API int q35_topk_fwd(const float *x, float *vals, int64_t *idx, int64_t rows,
+                 int cols, int k, q35_stream_t stream);
+
+/* ---- Permutation ---------------------------------------------------------
+ * Sorts the T*k (token, slot) pairs of idx [T,k] by (expert, token): the order
+ * the reference's per-expert mask.nonzero loop visits them
+ * (REF modules/moe.py:71-76).  Outputs:
+ *   counts    int32 [E]        tokens routed to each expert
+ *   offsets   int32 [E+1]      exclusive prefix sum of counts
+ *   sorted_tok int32 [T*k]     token index of sorted row r
+ *   slot_pos  int32 [T*k]      sorted row of pair (t, j) at t*k + j
+ *   tile_offsets int32 [E+1]   prefix sum of ceil(counts[e] / 128), the
+ *                               grouped-GEMM M-tile schedule
+ * workspace: int32 scratch of q35_moe_permute_workspace(T, E) elements.
+ * Expert ids outside [0, E) are recorded in the device error word and the
+ * pair is dropped (slot_pos = -1).                                        */
+Q35_API int64_t q35_moe_permute_workspace(int64_t T, int E);
+Q35_API int q35_moe_permute(const int32_t *idx, int64_t T, int k, int E,
+                    int32_t *counts, int32_t *offsets, int32_t *sorted_tok,
+                    int32_t *slot_pos, int32_t *tile_offsets,
+                    int32_t *workspace, q35_stream_t stream);
+
+/* dst[r,:] = src[rows[r],:] for r < n (bf16, cols % 8 == 0); n may be read
+ * from device memory (n_dev != NULL: *n_dev rows, at most n_max).           */
+Q35_API int q35_gather_rows(const void *src, const int32_t *rows, void *dst,
+                    int64_t n_max, const int32_t *n_dev, int64_t cols,
+                    q35_stream_t stream);
+
+/* ---- GEMMs on tcgen05 (A, B K-major bf16, fp32 accumulate in TMEM) -------
+ * Dense: out[m,n] = sum_k a[m,k] * b[n,k]  (+ residual[m,n]) , bf16 out.
+ * Replaces matmul_forward(x, weight, bias) (REF csrc/matmul_op.cpp:11-14,
+ * csrc/matmul_op.cu:15-149) for the q/k/v/o projections; bias may be NULL
+ * (bf16 [N]); residual may be NULL (bf16 [M,N], fuses residual_add,
+ * REF csrc/residual_add_op.cpp:5-7).  K % 64 == 0, N % 16 == 0.             */
+Q35_API int q35_gemm_bf16(const void *a, const void *b, const void *bias,
+                  const void *residual, void *out, int64_t M, int64_t N,
+                  int64_t K, q35_stream_t stream);
+
+/* Grouped expert GEMMs over the permuted rows of q35_moe_permute.
+ * Group e owns rows [offsets[e], offsets[e+1]) of a (rows sorted by expert).
+ * gate_up: act[r, j] = bf16( silu(g) * u ), g = a[r,:].w[e, j, :],
+ *          u = a[r,:].w[e, I + j, :]; w = gate_up_proj [E, 2I, H], act [R, I].
+ *          Replaces matmul(x_sub, gate_up_proj[e]) + swiglu (REF
+ *          modules/moe.py:77-80, csrc/swiglu_op.cu:6-18).
+ * down:    y[r, n] = bf16( act[r,:].w[e, n, :] ); w = down_proj [E, H, I].
+ *          Replaces matmul(activated, down_proj[e]) (REF modules/moe.py:81).
+ * offsets/tile_offsets are device arrays ([E+1]); rows_cap bounds R.        */
+Q35_API int q35_grouped_gemm_gateup_swiglu(const void *a, const void *w_gate_up,
+                                   void *act, const int32_t *offsets,
+                                   const int32_t *tile_offsets, int E,
+                                   int64_t rows_cap, int H, int I,
+                                   q35_stream_t stream);
+Q35_API int q35_grouped_gemm_down(const void *act, const void *w_down, void *y,
+                          const int32_t *offsets, const int32_t *tile_offsets,
+                          int E, int64_t rows_cap, int H, int I,
+                          q35_stream_t stream);
+
+/* ---- Combine --------------------------------------------------------------
+ * out[t,:] = bf16( residual[t,:] + sum_j weights[t,j] * y[slot_pos[t*k+j],:] )
+ * summed in fp32 in slot order; residual may be NULL.  slot_pos < 0 marks a
+ * slot whose row lives on another rank (skipped).  Replaces the weighted
+ * index_add_forward + residual_add_forward pair (REF modules/moe.py:82-83,
+ * csrc/moe_routing_op.cpp:9-13, modules/text_decoder.py:64).                 */
+Q35_API int q35_moe_combine(const void *y, const float *weights,
+                    const int32_t *slot_pos, const void *residual, void *out,
+                    int64_t T, int k, int64_t H, q35_stream_t stream);
+
+/* target[index[r],:] += source[r,:] (bf16 or fp32 rows by dtype code:
+ * 0 = fp32, 1 = bf16), replaces index_add_forward
+ * (REF csrc/moe_routing_op.cpp:9-13, csrc/moe_routing_op.cu:89-102).       */
+Q35_API int q35_index_add(void *target, const void *source, const int64_t *index,
+                  int64_t n_src, int64_t n_target, int64_t cols, int dtype,
+                  q35_stream_t stream);
+
+/* Elementwise ops of the reference op layer (bf16): swiglu_forward
+ * (REF csrc/swiglu_op.cpp:8-11) and residual_add_forward
+ * (REF csrc/residual_add_op.cpp:5-7).                                        */
+Q35_API int q35_swiglu_fwd(const void *gate, const void *up, void *out, int64_t n,
+                   q35_stream_t stream);
+Q35_API int q35_residual_add_fwd(const void *a, const void *b, void *out, int64_t n,
+                         q35_stream_t stream);
+
+/* ---- Attention ------------------------------------------------------------
+ * Prefill: out[b, s, h*D + d] = softmax(q.k^T * scale + mask) . v, GQA with
+ * Hq/Hkv query heads per kv head, causal mask bottom-right aligned
+ * (query i of Sq sees keys j <= i + Skv - Sq).  q [B,Hq,Sq,D],
+ * k/v [B,Hkv,Skv,D] head-major bf16; out token-major bf16 [B,Sq,Hq*D];
+ * lse (fp32 [B,Hq,Sq], may be NULL).  D in {32, 64, 128}.
+ * Replaces flash_attention_forward(q, k, v, scale, is_causal, num_kv_groups)
+ *   REF csrc/flash_attention_op.cpp:13-16, csrc/flash_attention_op.cu:17-180. */
+Q35_API int q35_attn_prefill_fwd(const void *q, const void *k, const void *v,
+                         void *out, float *lse, int64_t B, int Hq, int Hkv,
+                         int64_t Sq, int64_t Skv, int D, float scale,
+                         int causal, q35_stream_t stream);
+
+/* Decode (Sq small, long Skv): split-KV attention with an LSE merge.
+ * Same layouts as prefill; non-causal over all Skv keys (the reference's
+ * S_q != S_k rule, REF modules/attention.py:95).  Sq <= 16.
+ * workspace: fp32 scratch of q35_attn_decode_workspace(...) floats.          */
+Q35_API int64_t q35_attn_decode_workspace(int64_t B, int Hq, int64_t Sq, int64_t Skv,
+                                  int D);
+Q35_API int q35_attn_decode_fwd(const void *q, const void *k, const void *v, void *out,
+                        int64_t B, int Hq, int Hkv, int64_t Sq, int64_t Skv,
+                        int D, float scale, float *workspace,
+                        q35_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q35B200_H */

@@ -1,0 +1,468 @@
+// Persistent tcgen05 GEMM for the dense projections and the grouped expert
+// GEMMs (gate_up with SwiGLU fused into the epilogue, down).
+//
+//   C[m, n] = sum_k A[m, k] * B[n, k]        A, B bf16 K-major, fp32 in TMEM
+//
+// One CTA per SM (192 threads, 6 warps) loops over output tiles 128 x BN:
+//   warp 0  lane 0 : TMA producer.  A tile 128 x 64 and B tile BN x 64 per
+//                    k-block into a STAGES-deep shared-memory ring
+//                    (128-byte swizzle, the layout UMMA reads directly).
+//   warp 1  lane 0 : MMA issuer.  4 x tcgen05.mma (K = 16 each) per k-block
+//                    into one of two TMEM accumulators (2 x BN fp32 columns),
+//                    tcgen05.commit releases the smem stage / publishes the
+//                    accumulator.  Warp 1 also owns the TMEM allocation.
+//   warps 2-5      : epilogue.  tcgen05.ld of the accumulator rows (warp w
+//                    reads TMEM lanes 32*(w%4)..+31 = tile rows), fused
+//                    bias / residual / SwiGLU math, bf16 stores.  The second
+//                    accumulator lets the epilogue of tile i overlap the MMAs
+//                    of tile i+1.
+//
+// Grouped mode: rows of A are the permuted (expert-sorted) token rows; group e
+// owns rows [offsets[e], offsets[e+1]) and ceil(count/128) M tiles
+// (tile_offsets, built by q35_moe_permute).  Tiles are ordered
+// (group, n-tile, m-tile) with m fastest, so CTAs running at the same time
+// share each weight tile through L2.  The tile count is read from device
+// memory: no host synchronisation is needed between routing and the GEMM.
+//
+// Reference counterparts: matmul_fwd_kernel (REF cuda_qwen3_vl/csrc/
+// matmul_op.cu:15-92, SIMT 32x32 tiles) for every projection, and the
+// per-expert loop of CudaSparseMoE.forward (REF modules/moe.py:71-83) with
+// swiglu_fwd_kernel (REF csrc/swiglu_op.cu:6-18) for the experts.
+#include "sm100.cuh"
+
+namespace q35 {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 bf16 = one 128-byte swizzle row
+constexpr int kThreads = 192;
+constexpr int kMaxGroups = 512;
+
+enum Epilogue { EPI_PLAIN = 0, EPI_SWIGLU = 1 };
+
+struct GemmParams {
+  int M;                       // dense rows (grouped: unused)
+  const int32_t *offsets;      // grouped: [E+1] row offsets, else nullptr
+  const int32_t *tile_offsets; // grouped: [E+1] M-tile prefix
+  int E;                       // groups (1 for dense)
+  int N;                       // valid output columns per group
+  int K;
+  int n_tiles;                 // tiles along N per group
+  int b_rows_per_group;        // rows of B owned by one group
+  int b_tile_step;             // B row advance per n-tile
+  int b_second_off;            // row offset of the second half box of B
+  uint16_t *out;
+  int64_t ldo;
+  const uint16_t *bias;        // [N] or nullptr
+  const uint16_t *residual;    // [rows, ldr] or nullptr
+  int64_t ldr;
+  int *err;
+};
+
+template <int BN, int STAGES>
+struct SmemLayout {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOff = STAGES * kStageBytes;
+  // full[S], empty[S], tfull[2], tempty[2], drain
+  static constexpr int kNumBars = 2 * STAGES + 5;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kGroupOff = kMiscOff + 16;
+  static constexpr int bytes(int E) {
+    return 1024 + kGroupOff + 2 * (E + 1) * 4;
+  }
+};
+
+struct TileInfo {
+  int row0;        // first A row of the tile
+  int rows_valid;  // rows of the tile that belong to the group
+  int group;
+  int nt;          // n-tile index
+};
+
+__device__ __forceinline__ TileInfo decode_tile(int tile, const GemmParams &p,
+                                                const int *s_off,
+                                                const int *s_toff) {
+  TileInfo ti;
+  if (p.offsets == nullptr) {
+    const int mtiles = (p.M + kBM - 1) / kBM;
+    ti.nt = tile / mtiles;
+    const int mt = tile - ti.nt * mtiles;
+    ti.group = 0;
+    ti.row0 = mt * kBM;
+    ti.rows_valid = min(kBM, p.M - ti.row0);
+    return ti;
+  }
+  // Largest e with s_toff[e] * n_tiles <= tile.
+  int lo = 0, hi = p.E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_toff[mid] * p.n_tiles <= tile)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  // Skip empty groups that share the same prefix (they own no tiles).
+  while (lo < p.E - 1 && s_toff[lo + 1] * p.n_tiles <= tile) ++lo;
+  const int e = lo;
+  const int me = s_toff[e + 1] - s_toff[e];
+  const int local = tile - s_toff[e] * p.n_tiles;
+  ti.nt = local / me;
+  const int mt = local - ti.nt * me;
+  ti.group = e;
+  ti.row0 = s_off[e] + mt * kBM;
+  ti.rows_valid = min(kBM, s_off[e + 1] - ti.row0);
+  return ti;
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+
+// Stores 32 consecutive bf16 outputs (fp32 values in v) at dst.
+__device__ __forceinline__ void store32(uint16_t *dst, const float *v) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 u;
+    u.x = pack_bf2(v[8 * q + 0], v[8 * q + 1]);
+    u.y = pack_bf2(v[8 * q + 2], v[8 * q + 3]);
+    u.z = pack_bf2(v[8 * q + 4], v[8 * q + 5]);
+    u.w = pack_bf2(v[8 * q + 6], v[8 * q + 7]);
+    reinterpret_cast<uint4 *>(dst)[q] = u;
+  }
+}
+__device__ __forceinline__ void load32(const uint16_t *src, float *v) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 u = reinterpret_cast<const uint4 *>(src)[q];
+    unpack_bf2(u.x, v[8 * q + 0], v[8 * q + 1]);
+    unpack_bf2(u.y, v[8 * q + 2], v[8 * q + 3]);
+    unpack_bf2(u.z, v[8 * q + 4], v[8 * q + 5]);
+    unpack_bf2(u.w, v[8 * q + 6], v[8 * q + 7]);
+  }
+}
+
+template <int BN, int EPI, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                   const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  using L = SmemLayout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBarOff);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + STAGES;
+  uint64_t *tfull = bars + 2 * STAGES;
+  uint64_t *tempty = bars + 2 * STAGES + 2;
+  uint64_t *drain = bars + 2 * STAGES + 4;
+  uint32_t *s_tmem = reinterpret_cast<uint32_t *>(smem + L::kMiscOff);
+  int *s_off = reinterpret_cast<int *>(smem + L::kGroupOff);
+  int *s_toff = s_off + (p.E + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (p.offsets != nullptr) {
+    for (int i = threadIdx.x; i <= p.E; i += kThreads) {
+      s_off[i] = p.offsets[i];
+      s_toff[i] = p.tile_offsets[i];
+    }
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      sm100::mbar_init(&full[s], 1);
+      sm100::mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(&tfull[a], 1);
+      sm100::mbar_init(&tempty[a], 128);
+    }
+    sm100::mbar_init(drain, 1);
+    sm100::fence_mbar_init();
+    sm100::prefetch_tensormap(&tmA);
+    sm100::prefetch_tensormap(&tmB);
+  }
+  if (warp == 1) sm100::tmem_alloc(s_tmem, 2 * BN);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+
+  int total;
+  if (p.offsets == nullptr)
+    total = ((p.M + kBM - 1) / kBM) * p.n_tiles;
+  else
+    total = s_toff[p.E] * p.n_tiles;
+
+  const int k_blocks = p.K / kBK;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------ TMA producer
+    uint32_t g = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+      const TileInfo ti = decode_tile(tile, p, s_off, s_toff);
+      const int brow = ti.group * p.b_rows_per_group + ti.nt * p.b_tile_step;
+      for (int kb = 0; kb < k_blocks; ++kb, ++g) {
+        const int s = g % STAGES;
+        const uint32_t ph = (g / STAGES) & 1u;
+        if (!sm100::mbar_wait(&empty[s], ph ^ 1u)) {
+          report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 201, tile, kb);
+          ok = false;
+          break;
+        }
+        uint8_t *sa = smem + s * L::kStageBytes;
+        uint8_t *sb = sa + L::kABytes;
+        sm100::mbar_arrive_expect_tx(&full[s], L::kStageBytes);
+        sm100::tma_load_2d(sa, &tmA, &full[s], kb * kBK, ti.row0);
+        sm100::tma_load_2d(sb, &tmB, &full[s], kb * kBK, brow);
+        sm100::tma_load_2d(sb + L::kBBytes / 2, &tmB, &full[s], kb * kBK,
+                           brow + p.b_second_off);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = sm100::idesc_bf16_f32(kBM, BN);
+    uint32_t g = 0, j = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++j) {
+      const uint32_t acc = j & 1u, use = j >> 1;
+      if (!sm100::mbar_wait(&tempty[acc], (use & 1u) ^ 1u)) {
+        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 202, tile, 0);
+        break;
+      }
+      sm100::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < k_blocks; ++kb, ++g) {
+        const int s = g % STAGES;
+        const uint32_t ph = (g / STAGES) & 1u;
+        if (!sm100::mbar_wait(&full[s], ph)) {
+          report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 203, tile, kb);
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t sa = sm100::smem_u32(smem + s * L::kStageBytes);
+        const uint64_t adesc = sm100::sw128_kmajor_desc(sa);
+        const uint64_t bdesc = sm100::sw128_kmajor_desc(sa + L::kABytes);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          sm100::mma_bf16_ss(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc,
+                             (kb | kk) != 0 ? 1u : 0u);
+        sm100::mma_commit(&empty[s]);
+      }
+      sm100::mma_commit(&tfull[acc]);
+    }
+    // Drain: every MMA issued above has finished before TMEM is released.
+    sm100::mma_commit(drain);
+    if (!sm100::mbar_wait(drain, 0))
+      report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 204, 0, 0);
+  } else if (warp >= 2) {
+    // ------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int r_in_tile = q * 32 + lane;
+    uint32_t j = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++j) {
+      const TileInfo ti = decode_tile(tile, p, s_off, s_toff);
+      const uint32_t acc = j & 1u, use = j >> 1;
+      if (!sm100::mbar_wait(&tfull[acc], use & 1u)) {
+        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 205, tile, 0);
+        break;
+      }
+      sm100::tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                             acc * BN;
+      const bool valid = r_in_tile < ti.rows_valid;
+      const int64_t row = static_cast<int64_t>(ti.row0) + r_in_tile;
+      if constexpr (EPI == EPI_PLAIN) {
+        const int n0 = ti.nt * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld32(t_row + c * 32, r);
+          sm100::tmem_wait_ld();
+          const int col = n0 + c * 32;
+          if (valid && col < p.N) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            if (p.bias) {
+              float bv[32];
+              load32(p.bias + col, bv);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] += bv[i];
+            }
+            if (p.residual) {
+              float rv[32];
+              load32(p.residual + row * p.ldr + col, rv);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = rv[i] + v[i];
+            }
+            store32(p.out + row * p.ldo + col, v);
+          }
+        }
+      } else {
+        // Accumulator columns [0, BN/2) hold gate, [BN/2, BN) the matching up.
+        const int n0 = ti.nt * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t rg[32], ru[32];
+          sm100::tmem_ld32(t_row + c * 32, rg);
+          sm100::tmem_ld32(t_row + BN / 2 + c * 32, ru);
+          sm100::tmem_wait_ld();
+          const int col = n0 + c * 32;
+          if (valid && col < p.N) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              v[i] = silu(__uint_as_float(rg[i])) * __uint_as_float(ru[i]);
+            store32(p.out + row * p.ldo + col, v);
+          }
+        }
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+template <int BN, int EPI, int STAGES>
+int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb,
+                const GemmParams &p, int max_tiles, cudaStream_t s) {
+  using L = SmemLayout<BN, STAGES>;
+  const int smem = L::bytes(p.E);
+  auto kern = gemm_tc_kernel<BN, EPI, STAGES>;
+  Q35_CHECK_CUDA(cudaFuncSetAttribute(
+      kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int grid = max(1, min(max_tiles, num_sms()));
+  kern<<<grid, kThreads, smem, s>>>(ta, tb, p);
+  Q35_LAUNCH_CHECK("gemm_tc launch");
+  return Q35_OK;
+}
+
+}  // namespace
+}  // namespace q35
+
+using namespace q35;
+
+extern "C" int q35_gemm_bf16(const void *a, const void *b, const void *bias,
+                             const void *residual, void *out, int64_t M,
+                             int64_t N, int64_t K, q35_stream_t stream) {
+  if (!a || !b || !out) return fail(Q35_ERR_INVALID, "gemm: null pointer");
+  if (M < 0 || N <= 0 || K <= 0) return fail(Q35_ERR_SHAPE, "gemm: bad shape");
+  if (K % kBK != 0 || N % 32 != 0)
+    return fail(Q35_ERR_SHAPE, "gemm: K %lld must be x64 and N %lld x32",
+                (long long)K, (long long)N);
+  if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 24))
+    return fail(Q35_ERR_SHAPE, "gemm: M/N too large");
+  if (!aligned16(out) || (residual && !aligned16(residual)) ||
+      (bias && !aligned16(bias)))
+    return fail(Q35_ERR_ALIGN, "gemm: out/bias/residual not 16-byte aligned");
+  if (M == 0) return Q35_OK;
+  int *err = device_error_word();
+  if (!err) return fail(Q35_ERR_CUDA, "gemm: no device error word");
+  const int sms = num_sms();
+  const int64_t mt = (M + kBM - 1) / kBM;
+  // Pick the N tile that finishes the last wave soonest (time ~ waves * BN).
+  const int64_t t256 = mt * ((N + 255) / 256), t128 = mt * ((N + 127) / 128);
+  const int64_t cost256 = ((t256 + sms - 1) / sms) * 2, cost128 = (t128 + sms - 1) / sms;
+  const int BN = (cost256 <= cost128 && N % 256 == 0) ? 256 : 128;
+  CUtensorMap ta, tb;
+  int st = make_tmap_bf16_2d(&ta, a, K, M, K * 2, kBK, kBM);
+  if (st) return st;
+  st = make_tmap_bf16_2d(&tb, b, K, N, K * 2, kBK, BN / 2);
+  if (st) return st;
+  GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.E = 1;
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.n_tiles = static_cast<int>((N + BN - 1) / BN);
+  p.b_rows_per_group = static_cast<int>(N);
+  p.b_tile_step = BN;
+  p.b_second_off = BN / 2;
+  p.out = static_cast<uint16_t *>(out);
+  p.ldo = N;
+  p.bias = static_cast<const uint16_t *>(bias);
+  p.residual = static_cast<const uint16_t *>(residual);
+  p.ldr = N;
+  p.err = err;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int tiles = static_cast<int>(mt * p.n_tiles);
+  if (BN == 256) return launch_gemm<256, EPI_PLAIN, 4>(ta, tb, p, tiles, s);
+  return launch_gemm<128, EPI_PLAIN, 6>(ta, tb, p, tiles, s);
+}
+
+static int grouped_common(const void *a, const void *w, void *out,
+                          const int32_t *offsets, const int32_t *tile_offsets,
+                          int E, int64_t rows_cap, int64_t K, int64_t N_out,
+                          int64_t b_rows_per_group, int swiglu,
+                          q35_stream_t stream) {
+  if (!a || !w || !out || !offsets || !tile_offsets)
+    return fail(Q35_ERR_INVALID, "grouped_gemm: null pointer");
+  if (E < 1 || E > kMaxGroups)
+    return fail(Q35_ERR_SHAPE, "grouped_gemm: groups %d (1..%d)", E, kMaxGroups);
+  if (rows_cap < 0 || rows_cap >= (int64_t(1) << 31))
+    return fail(Q35_ERR_SHAPE, "grouped_gemm: rows_cap out of range");
+  if (K % kBK != 0 || N_out % 32 != 0)
+    return fail(Q35_ERR_SHAPE, "grouped_gemm: K %lld (x64) / N %lld (x32)",
+                (long long)K, (long long)N_out);
+  if (!aligned16(out)) return fail(Q35_ERR_ALIGN, "grouped_gemm: out alignment");
+  if (rows_cap == 0) return Q35_OK;
+  int *err = device_error_word();
+  if (!err) return fail(Q35_ERR_CUDA, "grouped_gemm: no device error word");
+  constexpr int BN = 256;
+  CUtensorMap ta, tb;
+  int st = make_tmap_bf16_2d(&ta, a, K, rows_cap, K * 2, kBK, kBM);
+  if (st) return st;
+  st = make_tmap_bf16_2d(&tb, w, K, static_cast<uint64_t>(E) * b_rows_per_group,
+                         K * 2, kBK, BN / 2);
+  if (st) return st;
+  GemmParams p{};
+  p.offsets = offsets;
+  p.tile_offsets = tile_offsets;
+  p.E = E;
+  p.N = static_cast<int>(N_out);
+  p.K = static_cast<int>(K);
+  p.n_tiles = static_cast<int>(swiglu ? (N_out + BN / 2 - 1) / (BN / 2)
+                                      : (N_out + BN - 1) / BN);
+  p.b_rows_per_group = static_cast<int>(b_rows_per_group);
+  p.b_tile_step = swiglu ? BN / 2 : BN;
+  p.b_second_off = swiglu ? static_cast<int>(N_out) : BN / 2;
+  p.out = static_cast<uint16_t *>(out);
+  p.ldo = N_out;
+  p.err = err;
+  // Upper bound on tiles: every group may add one partial M tile.
+  const int64_t max_tiles = ((rows_cap + kBM - 1) / kBM + E) * p.n_tiles;
+  const int mt = static_cast<int>(max_tiles < (1 << 30) ? max_tiles : (1 << 30));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (swiglu) return launch_gemm<BN, EPI_SWIGLU, 4>(ta, tb, p, mt, s);
+  return launch_gemm<BN, EPI_PLAIN, 4>(ta, tb, p, mt, s);
+}
+
+extern "C" int q35_grouped_gemm_gateup_swiglu(
+    const void *a, const void *w_gate_up, void *act, const int32_t *offsets,
+    const int32_t *tile_offsets, int E, int64_t rows_cap, int H, int I,
+    q35_stream_t stream) {
+  if (H <= 0 || I <= 0) return fail(Q35_ERR_SHAPE, "gate_up: bad H/I");
+  return grouped_common(a, w_gate_up, act, offsets, tile_offsets, E, rows_cap,
+                        H, I, 2 * static_cast<int64_t>(I), 1, stream);
+}
+
+extern "C" int q35_grouped_gemm_down(const void *act, const void *w_down,
+                                     void *y, const int32_t *offsets,
+                                     const int32_t *tile_offsets, int E,
+                                     int64_t rows_cap, int H, int I,
+                                     q35_stream_t stream) {
+  if (H <= 0 || I <= 0) return fail(Q35_ERR_SHAPE, "down: bad H/I");
+  return grouped_common(act, w_down, y, offsets, tile_offsets, E, rows_cap, I,
+                        H, H, 0, stream);
+}

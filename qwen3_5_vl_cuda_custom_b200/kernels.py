@@ -1,0 +1,344 @@
+"""Operator layer: the reference's op wrappers, re-implemented on libq35b200.
+
+The reference exposes one Python function per op (REF cuda_qwen3_vl/kernels/
+__init__.py:1-45), each falling back to torch when the tensor is not on CUDA
+or the JIT build fails (e.g. REF kernels/matmul.py:62-77).  The functions here
+keep the names and argument meanings, but they have no fallback: they require
+CUDA tensors of the supported dtype and raise otherwise.  Fused entry points
+used by the modules (router, permutation, grouped GEMMs, combine, QK-norm +
+mRoPE) live here too.
+
+Tensors passed in are made contiguous; outputs are allocated with
+``torch.empty`` on the input's device and the work is enqueued on the current
+CUDA stream.
+"""
+from __future__ import annotations
+
+
+import torch
+
+from . import _lib
+
+_BF16 = torch.bfloat16
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _require(t: torch.Tensor, name: str, dtype: torch.dtype | tuple = _BF16) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name}: expected a tensor")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name}: CUDA tensor required (this library has no CPU path)")
+    dts = dtype if isinstance(dtype, tuple) else (dtype,)
+    if t.dtype not in dts:
+        raise RuntimeError(f"{name}: dtype {t.dtype} unsupported (expected {dts})")
+    return t.contiguous()
+
+
+# ---------------------------------------------------------------- norms
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """RMSNorm over the last dim (REF kernels/rmsnorm.py:66-77). bf16 only."""
+    x = _require(x, "rmsnorm.x")
+    weight = _require(weight.to(x.dtype) if weight.dtype != x.dtype else weight, "rmsnorm.weight")
+    cols = x.shape[-1]
+    if weight.numel() != cols:
+        raise RuntimeError(f"rmsnorm: weight has {weight.numel()} elements, x has {cols} columns")
+    y = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        _lib.call("q35_rmsnorm_fwd", x.data_ptr(), weight.data_ptr(), y.data_ptr(),
+                  x.numel() // cols if cols else 0, cols, float(eps), _stream(x))
+    return y
+
+
+# ---------------------------------------------------------------- GEMM
+def matmul(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+           residual: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ weight^T (+ bias) (+ residual), REF kernels/matmul.py:62-77.
+
+    bf16 in and out, fp32 accumulation on tcgen05.  ``residual`` (same shape as
+    the output) fuses the reference's residual_add into the GEMM epilogue.
+    """
+    x = _require(x, "matmul.x")
+    weight = _require(weight, "matmul.weight")
+    K = x.shape[-1]
+    N, Kw = weight.shape
+    if Kw != K:
+        raise RuntimeError(f"matmul: x has K={K}, weight has K={Kw}")
+    M = x.numel() // K if K else 0
+    out = torch.empty(*x.shape[:-1], N, device=x.device, dtype=x.dtype)
+    if bias is not None:
+        bias = _require(bias, "matmul.bias")
+    if residual is not None:
+        residual = _require(residual, "matmul.residual")
+        if residual.shape != out.shape:
+            raise RuntimeError("matmul: residual shape must equal the output shape")
+    with torch.cuda.device(x.device):
+        _lib.call("q35_gemm_bf16", x.data_ptr(), weight.data_ptr(), _ptr(bias), _ptr(residual),
+                  out.data_ptr(), M, N, K, _stream(x))
+    return out
+
+
+# ---------------------------------------------------------------- routing
+def softmax(x: torch.Tensor) -> torch.Tensor:
+    """Row softmax over the last dim in fp32 (REF kernels/softmax.py:40-51)."""
+    x = _require(x, "softmax.x", torch.float32)
+    y = torch.empty_like(x)
+    cols = x.shape[-1]
+    with torch.cuda.device(x.device):
+        _lib.call("q35_softmax_fwd", x.data_ptr(), y.data_ptr(), x.numel() // cols, cols, _stream(x))
+    return y
+
+
+def cuda_topk(x: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Top-k over the last dim, sorted descending, ties to the lower index
+    (REF kernels/moe_routing.py:55-67).  Returns (values fp32, indices int64)."""
+    x = _require(x, "cuda_topk.x", torch.float32)
+    cols = x.shape[-1]
+    rows = x.numel() // cols
+    vals = torch.empty(*x.shape[:-1], k, device=x.device, dtype=torch.float32)
+    idx = torch.empty(*x.shape[:-1], k, device=x.device, dtype=torch.int64)
+    with torch.cuda.device(x.device):
+        _lib.call("q35_topk_fwd", x.data_ptr(), vals.data_ptr(), idx.data_ptr(), rows, cols, int(k),
+                  _stream(x))
+    return vals, idx
+
+
+def cuda_index_add(target: torch.Tensor, source: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
+    """target[index[r]] += source[r], in place (REF kernels/moe_routing.py:103-121)."""
+    if not target.is_contiguous():
+        raise RuntimeError("cuda_index_add: target must be contiguous (it is updated in place)")
+    _require(target, "cuda_index_add.target", (torch.float32, _BF16))
+    source = _require(source.to(target.dtype), "cuda_index_add.source", target.dtype)
+    index = _require(index.to(torch.int64), "cuda_index_add.index", torch.int64)
+    cols = target[0].numel() if target.shape[0] else 0
+    code = 0 if target.dtype == torch.float32 else 1
+    with torch.cuda.device(target.device):
+        _lib.call("q35_index_add", target.data_ptr(), source.data_ptr(), index.data_ptr(),
+                  index.numel(), target.shape[0], cols, code, _stream(target))
+    return target
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """silu(gate) * up, elementwise (REF kernels/swiglu.py:56-67)."""
+    gate = _require(gate, "swiglu.gate")
+    up = _require(up, "swiglu.up")
+    out = torch.empty_like(gate)
+    with torch.cuda.device(gate.device):
+        _lib.call("q35_swiglu_fwd", gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel(),
+                  _stream(gate))
+    return out
+
+
+def residual_add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a + b elementwise (REF kernels/residual_add.py)."""
+    a = _require(a, "residual_add.a")
+    b = _require(b, "residual_add.b")
+    out = torch.empty_like(a)
+    with torch.cuda.device(a.device):
+        _lib.call("q35_residual_add_fwd", a.data_ptr(), b.data_ptr(), out.data_ptr(), a.numel(),
+                  _stream(a))
+    return out
+
+
+def router_topk(x2d: torch.Tensor, gate_weight: torch.Tensor, top_k: int, renorm: bool = True,
+                bias: torch.Tensor | None = None):
+    """Fused fp32 router: logits (T,E) fp32, top-k ids (T,k) int32, weights (T,k) fp32."""
+    x2d = _require(x2d, "router.x")
+    wg = _require(gate_weight, "router.gate_weight", torch.float32)
+    T, H = x2d.shape
+    E = wg.shape[0]
+    logits = torch.empty(T, E, device=x2d.device, dtype=torch.float32)
+    idx = torch.empty(T, top_k, device=x2d.device, dtype=torch.int32)
+    w = torch.empty(T, top_k, device=x2d.device, dtype=torch.float32)
+    if bias is not None:
+        bias = _require(bias, "router.bias", torch.float32)
+    with torch.cuda.device(x2d.device):
+        _lib.call("q35_router_topk_fwd", x2d.data_ptr(), wg.data_ptr(), _ptr(bias), logits.data_ptr(),
+                  idx.data_ptr(), w.data_ptr(), T, H, E, int(top_k), 1 if renorm else 0, _stream(x2d))
+    return logits, idx, w
+
+
+class Permutation:
+    """Device arrays of the (expert, token) sort of the routed pairs."""
+
+    __slots__ = ("counts", "offsets", "sorted_tok", "slot_pos", "tile_offsets", "num_experts")
+
+    def __init__(self, counts, offsets, sorted_tok, slot_pos, tile_offsets, num_experts):
+        self.counts = counts
+        self.offsets = offsets
+        self.sorted_tok = sorted_tok
+        self.slot_pos = slot_pos
+        self.tile_offsets = tile_offsets
+        self.num_experts = num_experts
+
+
+def moe_permute(idx: torch.Tensor, num_experts: int) -> Permutation:
+    """Stable (expert, token) sort of top-k ids idx (T,k) int32 (REF modules/moe.py:71-76)."""
+    idx = _require(idx, "moe_permute.idx", torch.int32)
+    T, k = idx.shape
+    dev = idx.device
+    i32 = dict(device=dev, dtype=torch.int32)
+    counts = torch.empty(num_experts, **i32)
+    offsets = torch.empty(num_experts + 1, **i32)
+    tile_offsets = torch.empty(num_experts + 1, **i32)
+    sorted_tok = torch.empty(T * k, **i32)
+    slot_pos = torch.empty(T * k, **i32)
+    ws = torch.empty(max(1, _lib.query("q35_moe_permute_workspace", T, num_experts)), **i32)
+    with torch.cuda.device(dev):
+        _lib.call("q35_moe_permute", idx.data_ptr(), T, k, num_experts, counts.data_ptr(),
+                  offsets.data_ptr(), sorted_tok.data_ptr(), slot_pos.data_ptr(),
+                  tile_offsets.data_ptr(), ws.data_ptr(), _stream(idx))
+    return Permutation(counts, offsets, sorted_tok, slot_pos, tile_offsets, num_experts)
+
+
+def gather_rows(src: torch.Tensor, rows: torch.Tensor, n_dev: torch.Tensor | None = None) -> torch.Tensor:
+    """dst[r] = src[rows[r]] for bf16 rows (rows int32); n_dev (device int32) bounds r."""
+    src = _require(src, "gather_rows.src")
+    rows = _require(rows, "gather_rows.rows", torch.int32)
+    n = rows.numel()
+    cols = src.shape[-1]
+    dst = torch.empty(n, cols, device=src.device, dtype=src.dtype)
+    with torch.cuda.device(src.device):
+        _lib.call("q35_gather_rows", src.data_ptr(), rows.data_ptr(), dst.data_ptr(), n,
+                  _ptr(n_dev), cols, _stream(src))
+    return dst
+
+
+def grouped_gateup_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, perm: Permutation,
+                          rows_cap: int | None = None) -> torch.Tensor:
+    """act[r] = silu(a[r] @ Wg[e]^T) * (a[r] @ Wu[e]^T) for the rows of each expert e."""
+    a = _require(a, "gate_up.a")
+    w = _require(w_gate_up, "gate_up.w")
+    E, I2, H = w.shape
+    R = a.shape[0] if rows_cap is None else rows_cap
+    act = torch.empty(R, I2 // 2, device=a.device, dtype=a.dtype)
+    with torch.cuda.device(a.device):
+        _lib.call("q35_grouped_gemm_gateup_swiglu", a.data_ptr(), w.data_ptr(), act.data_ptr(),
+                  perm.offsets.data_ptr(), perm.tile_offsets.data_ptr(), E, R, H, I2 // 2,
+                  _stream(a))
+    return act
+
+
+def grouped_down(act: torch.Tensor, w_down: torch.Tensor, perm: Permutation) -> torch.Tensor:
+    """y[r] = act[r] @ Wd[e]^T for the rows of each expert e."""
+    act = _require(act, "down.act")
+    w = _require(w_down, "down.w")
+    E, H, I = w.shape
+    R = act.shape[0]
+    y = torch.empty(R, H, device=act.device, dtype=act.dtype)
+    with torch.cuda.device(act.device):
+        _lib.call("q35_grouped_gemm_down", act.data_ptr(), w.data_ptr(), y.data_ptr(),
+                  perm.offsets.data_ptr(), perm.tile_offsets.data_ptr(), E, R, H, I, _stream(act))
+    return y
+
+
+def moe_combine(y: torch.Tensor, weights: torch.Tensor, slot_pos: torch.Tensor,
+                residual: torch.Tensor | None, T: int, H: int) -> torch.Tensor:
+    """out[t] = residual[t] + sum_j weights[t,j] * y[slot_pos[t,j]] (fp32 sum, bf16 out)."""
+    y = _require(y, "combine.y")
+    weights = _require(weights, "combine.weights", torch.float32)
+    slot_pos = _require(slot_pos, "combine.slot_pos", torch.int32)
+    k = weights.shape[-1]
+    if residual is not None:
+        residual = _require(residual, "combine.residual")
+    out = torch.empty(T, H, device=weights.device, dtype=_BF16)
+    with torch.cuda.device(weights.device):
+        _lib.call("q35_moe_combine", y.data_ptr(), weights.data_ptr(), slot_pos.data_ptr(),
+                  _ptr(residual), out.data_ptr(), T, k, H, _stream(weights))
+    return out
+
+
+# ---------------------------------------------------------------- rotary
+def qknorm_mrope(qkv: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor,
+                 position_ids: torch.Tensor, inv_freq: torch.Tensor, mrope_section,
+                 B: int, S: int, Hq: int, Hkv: int, D: int, eps: float, interleaved: bool = False):
+    """Fused QK-RMSNorm + mRoPE + head-major split of the fused qkv projection."""
+    qkv = _require(qkv, "qknorm_mrope.qkv")
+    q_w = _require(q_w, "qknorm_mrope.q_w")
+    k_w = _require(k_w, "qknorm_mrope.k_w")
+    pos = _require(position_ids.to(torch.int64), "qknorm_mrope.position_ids", torch.int64)
+    inv = _require(inv_freq, "qknorm_mrope.inv_freq", torch.float32)
+    dev = qkv.device
+    q = torch.empty(B, Hq, S, D, device=dev, dtype=_BF16)
+    k = torch.empty(B, Hkv, S, D, device=dev, dtype=_BF16)
+    v = torch.empty(B, Hkv, S, D, device=dev, dtype=_BF16)
+    with torch.cuda.device(dev):
+        _lib.call("q35_qknorm_mrope_fwd", qkv.data_ptr(), q_w.data_ptr(), k_w.data_ptr(),
+                  pos.data_ptr(), inv.data_ptr(), _lib.sections_arg(mrope_section),
+                  1 if interleaved else 0, q.data_ptr(), k.data_ptr(), v.data_ptr(), B, S, Hq, Hkv,
+                  D, float(eps), _stream(qkv))
+    return q, k, v
+
+
+def mrope(x: torch.Tensor, position_ids: torch.Tensor, inv_freq: torch.Tensor, mrope_section,
+          interleaved: bool = False) -> torch.Tensor:
+    """mRoPE on a head-major (B,H,S,D) tensor, cos/sin computed on the fly from
+    (3,B,S) positions (replaces apply_mrope, REF kernels/mrope.py:80-104)."""
+    x = _require(x, "mrope.x")
+    pos = _require(position_ids.to(torch.int64), "mrope.position_ids", torch.int64)
+    inv = _require(inv_freq, "mrope.inv_freq", torch.float32)
+    B, H, S, D = x.shape
+    y = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        _lib.call("q35_mrope_fwd", x.data_ptr(), y.data_ptr(), pos.data_ptr(), inv.data_ptr(),
+                  _lib.sections_arg(mrope_section), 1 if interleaved else 0, B, H, S, D, _stream(x))
+    return y
+
+
+# ---------------------------------------------------------------- attention
+def attention_tokens(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+                     causal: bool) -> torch.Tensor:
+    """Attention of head-major q (B,Hq,Sq,D), k/v (B,Hkv,Skv,D); returns the
+    token-major (B,Sq,Hq*D) output that feeds o_proj directly.  Causal masking
+    is bottom-right aligned.  Decode-shaped calls use the split-KV kernel."""
+    q = _require(q, "attention.q")
+    k = _require(k, "attention.k")
+    v = _require(v, "attention.v")
+    B, Hq, Sq, D = q.shape
+    Hkv, Skv = k.shape[1], k.shape[2]
+    out = torch.empty(B, Sq, Hq * D, device=q.device, dtype=q.dtype)
+    with torch.cuda.device(q.device):
+        if (not causal or Sq == 1) and (Hq // Hkv) * Sq <= 16:
+            n = _lib.query("q35_attn_decode_workspace", B, Hq, Sq, Skv, D)
+            ws = torch.empty(max(1, n), device=q.device, dtype=torch.float32)
+            _lib.call("q35_attn_decode_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                      B, Hq, Hkv, Sq, Skv, D, float(scale), ws.data_ptr(), _stream(q))
+        else:
+            _lib.call("q35_attn_prefill_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                      out.data_ptr(), None, B, Hq, Hkv, Sq, Skv, D, float(scale),
+                      1 if causal else 0, _stream(q))
+    return out
+
+
+def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+                    is_causal: bool = True, num_kv_groups: int = 1) -> torch.Tensor:
+    """Reference op signature (REF kernels/flash_attention.py:82-100): returns
+    (B,Hq,Sq,D) (a view of the token-major result)."""
+    B, Hq, Sq, D = q.shape
+    if Hq != k.shape[1] * num_kv_groups:
+        raise RuntimeError("flash_attention: Hq must equal Hkv * num_kv_groups")
+    out = attention_tokens(q, k, v, scale, is_causal)
+    return out.view(B, Sq, Hq, D).transpose(1, 2)
+
+
+def default_scale(head_dim: int) -> float:
+    return head_dim ** -0.5
+
+
+def device_error_check():
+    """Synchronises and raises if any kernel recorded a device-side error."""
+    return _lib.device_error_check()
+
+
+__all__ = [
+    "rmsnorm", "matmul", "softmax", "cuda_topk", "cuda_index_add", "swiglu", "residual_add",
+    "router_topk", "moe_permute", "Permutation", "gather_rows", "grouped_gateup_swiglu",
+    "grouped_down", "moe_combine", "qknorm_mrope", "mrope", "attention_tokens",
+    "flash_attention", "device_error_check", "default_scale",
+]

@@ -1,0 +1,87 @@
+"""Qwen3-VL-MoE text stack (REF cuda_qwen3_vl/models/moe.py:18-100).
+
+``CudaQwen3VLMoeModel(cfg).forward(input_ids, pixel_values, vision_position_ids,
+image_token_mask, position_ids, past_key_values, return_kv)`` returns
+``(logits, router_logits_list[, new_kvs])`` like the reference.  The vision
+tower is outside this library's scope: ``pixel_values`` must be None (callers
+with image features pass them through ``inputs_embeds``, an extra keyword).
+"""
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from .configs import MoETextConfig, Qwen3VLConfig
+from .modules import CudaEmbedding, CudaLinear, CudaRMSNorm, CudaTextDecoderLayer, TextMRoPE
+
+
+def _layer_uses_moe(cfg: MoETextConfig, layer_idx: int) -> bool:
+    """MoE on layers with (i+1) % decoder_sparse_step == 0 outside mlp_only_layers
+    (REF models/moe.py:18-23)."""
+    if cfg.num_experts <= 0:
+        return False
+    if layer_idx in cfg.mlp_only_layers:
+        return False
+    return ((layer_idx + 1) % cfg.decoder_sparse_step) == 0
+
+
+class CudaQwen3VLMoeModel(nn.Module):
+    def __init__(self, cfg: Qwen3VLConfig) -> None:
+        super().__init__()
+        if cfg.family != "moe" or not isinstance(cfg.text, MoETextConfig):
+            raise ValueError(f"expected an MoE config, got {cfg.family}")
+        self.cfg = cfg
+        t = cfg.text
+        self.visual = None  # vision tower: not part of this library
+        self.embed_tokens = CudaEmbedding(t.vocab_size, t.hidden_size)
+        self.rotary = TextMRoPE(t.head_dim, theta=t.rope_theta, mrope_section=t.mrope_section)
+        self.layers = nn.ModuleList([
+            CudaTextDecoderLayer(
+                hidden_size=t.hidden_size, num_heads=t.num_heads, num_kv_heads=t.num_kv_heads,
+                head_dim=t.head_dim, intermediate_size=t.intermediate_size,
+                rms_norm_eps=t.rms_norm_eps, use_moe=_layer_uses_moe(t, i),
+                num_experts=t.num_experts, top_k=t.num_experts_per_tok,
+                moe_intermediate_size=t.moe_intermediate_size, attention_bias=t.attention_bias)
+            for i in range(t.num_layers)
+        ])
+        self.norm = CudaRMSNorm(t.hidden_size, eps=t.rms_norm_eps)
+        self.lm_head = CudaLinear(t.hidden_size, t.vocab_size, bias=False)
+        if t.tie_word_embeddings:
+            self.lm_head.weight = self.embed_tokens.weight
+
+    def _text_forward(self, input_embeds: torch.Tensor, position_ids: torch.Tensor,
+                      past_key_values=None):
+        x = input_embeds
+        mrope_fn = self.rotary.bind(position_ids)
+        router_logits_all: list[torch.Tensor] = []
+        new_kvs: list[tuple[torch.Tensor, torch.Tensor]] = []
+        for i, layer in enumerate(self.layers):
+            layer_past = past_key_values[i] if past_key_values is not None else None
+            x, rl, new_kv = layer(x, mrope_fn, past_kv=layer_past)
+            if rl is not None:
+                router_logits_all.append(rl)
+            new_kvs.append(new_kv)
+        return self.norm(x), router_logits_all, new_kvs
+
+    def forward(self, input_ids: torch.Tensor | None = None, pixel_values=None,
+                vision_position_ids=None, image_token_mask=None, position_ids=None,
+                past_key_values=None, return_kv: bool = False, inputs_embeds=None):
+        if pixel_values is not None:
+            raise NotImplementedError("the vision tower is not part of this library; "
+                                      "pass image features via inputs_embeds")
+        if inputs_embeds is None:
+            if input_ids is None:
+                raise ValueError("input_ids or inputs_embeds is required")
+            inputs_embeds = self.embed_tokens(input_ids)
+        B, S = inputs_embeds.shape[:2]
+        if position_ids is None:
+            past_len = past_key_values[0][0].shape[2] if past_key_values else 0
+            pos = torch.arange(past_len, past_len + S, device=inputs_embeds.device)
+            pos = pos.unsqueeze(0).expand(B, S)
+            position_ids = torch.stack([pos, pos, pos], dim=0)
+        hidden, router_logits, new_kvs = self._text_forward(inputs_embeds, position_ids,
+                                                            past_key_values=past_key_values)
+        logits = self.lm_head(hidden)
+        if return_kv:
+            return logits, router_logits, new_kvs
+        return logits, router_logits
