@@ -57,6 +57,11 @@ class ClockSampler:
         self.proc = None
         self.lines: list[str] = []
 
+    def wait_first(self, timeout: float = 5.0):
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < timeout and self.proc is not None:
+            time.sleep(0.05)
+
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
@@ -306,14 +311,15 @@ def run_ours(args, world, rank, local):
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
     bpos = rot.bind(pos)
 
-    with torch.no_grad():
-        # ---------------- warm-up (also JIT-free: the library is AOT)
+    with torch.no_grad(), ClockSampler(local) as clk:
+        clk.wait_first()
+        # ---------------- warm-up (the library is AOT-built: no JIT here)
         for _ in range(max(3, args.warmup)):
             layer(x, bpos)
         barrier(world)
         # ---------------- device-timed steps
         times = []
-        with ClockSampler(local) as clk:
+        if True:
             barrier(world)
             for _ in range(args.steps):
                 flush.zero_()

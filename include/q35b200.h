@@ -103,7 +103,7 @@ Q35_API int q35_mrope_fwd(const void *x, void *y, const int64_t *positions,
  * Replaces the router of CudaSparseMoE.forward (REF modules/moe.py:60-65):
  *   matmul_forward (csrc/matmul_op.cpp:11-14) -> softmax_forward
  *   (csrc/softmax_op.cpp:6-9) -> topk_forward (csrc/moe_routing_op.cpp:9-13).
- * bias may be NULL.  E <= 256, k <= 16, H % 8 == 0.
+ * bias may be NULL.  1 <= E <= 256, k <= 16, H % 32 == 0.
  * idx is int32 (the reference returns int64; values are equal).            */
 Q35_API int q35_router_topk_fwd(const void *x, const float *wg, const float *bias,
                         float *logits, int32_t *idx, float *weights,
@@ -152,7 +152,7 @@ Q35_API int q35_gather_rows(const void *src, const int32_t *rows, void *dst,
  * Replaces matmul_forward(x, weight, bias) (REF csrc/matmul_op.cpp:11-14,
  * csrc/matmul_op.cu:15-149) for the q/k/v/o projections; bias may be NULL
  * (bf16 [N]); residual may be NULL (bf16 [M,N], fuses residual_add,
- * REF csrc/residual_add_op.cpp:5-7).  K % 64 == 0, N % 16 == 0.             */
+ * REF csrc/residual_add_op.cpp:5-7).  K % 8 == 0, N % 32 == 0.             */
 Q35_API int q35_gemm_bf16(const void *a, const void *b, const void *bias,
                   const void *residual, void *out, int64_t M, int64_t N,
                   int64_t K, q35_stream_t stream);

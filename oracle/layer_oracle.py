@@ -144,11 +144,20 @@ def permutation(idx: np.ndarray, E: int, tile_m: int = 128):
     return counts, offsets, sorted_tok, slot_pos, tile_offsets
 
 
-def moe(x2d: torch.Tensor, wg, gate_up, down, k: int, renorm: bool = True, bias=None):
+def moe(x2d: torch.Tensor, wg, gate_up, down, k: int, renorm: bool = True, bias=None,
+        force_idx: torch.Tensor | None = None):
     """CudaSparseMoE.forward in fp32 (REF modules/moe.py:54-85).
+    ``force_idx`` (T,k) replaces the top-k choice (the weights are still the
+    oracle's own probabilities at those experts, renormalised): it isolates the
+    discrete routing decision when comparing against another implementation.
     Returns (out (T,H), logits (T,E), top_idx, top_w, probs)."""
     x2d = x2d.float()
     logits, p, idx, w = router(x2d, wg, k, renorm, bias)
+    if force_idx is not None:
+        idx = force_idx.long()
+        w = torch.gather(p, 1, idx)
+        if renorm:
+            w = w / w.sum(dim=-1, keepdim=True)
     I = gate_up.shape[1] // 2
     final = torch.zeros_like(x2d)
     for e in range(gate_up.shape[0]):
@@ -188,7 +197,7 @@ def attention_block(x: torch.Tensor, P: dict, cfg, position_ids, past_kv=None,
 
 
 def decoder_layer(x: torch.Tensor, P: dict, cfg, position_ids, past_kv=None,
-                  interleaved: bool = False, router_bias=None):
+                  interleaved: bool = False, router_bias=None, force_idx=None):
     """CudaTextDecoderLayer.forward for an MoE layer in fp32
     (REF modules/text_decoder.py:51-65).
     Returns dict(out, router_logits, top_idx, top_w, probs, k, v, h_attn)."""
@@ -200,7 +209,8 @@ def decoder_layer(x: torch.Tensor, P: dict, cfg, position_ids, past_kv=None,
     h = x + a
     m_in = rmsnorm(h, P["post_attention_layernorm.weight"], eps)
     mo, logits, idx, w, p = moe(m_in.reshape(-1, H), P["mlp.gate_weight"], P["mlp.gate_up_proj"],
-                                P["mlp.down_proj"], cfg.num_experts_per_tok, True, router_bias)
+                                P["mlp.down_proj"], cfg.num_experts_per_tok, True, router_bias,
+                                force_idx)
     out = h + mo.reshape(B, S, H)
     return dict(out=out, router_logits=logits, top_idx=idx, top_w=w, probs=p, k=k, v=v,
                 h_attn=h, moe_in=m_in)
@@ -216,12 +226,40 @@ def near_tie_rows(probs: torch.Tensor, k: int, rel: float = 1e-5) -> torch.Tenso
     return gap < rel * vals[..., k - 1]
 
 
+def bf16_half_ulp(v: torch.Tensor) -> torch.Tensor:
+    """Half a bf16 ulp at |v|: the rounding error any bf16 output must carry."""
+    a = v.float().abs().clamp_min(2.0 ** -126)
+    return torch.exp2(torch.floor(torch.log2(a)) - 8)
+
+
 def error_stats(got: torch.Tensor, ref: torch.Tensor) -> dict:
-    """max-abs error and mean relative error (sum|d| / sum|ref|)."""
-    d = (got.float() - ref.float()).abs()
+    """max-abs error, the same after removing the unavoidable bf16 output
+    rounding (max(0, |d| - half_ulp(ref))), and the mean relative error
+    sum|d| / sum|ref|."""
+    g, r = got.float(), ref.float()
+    d = (g - r).abs()
+    dq = (d - bf16_half_ulp(r)).clamp_min(0.0)
     return {"max_abs": float(d.max()) if d.numel() else 0.0,
-            "mean_rel": float(d.sum() / ref.float().abs().sum().clamp_min(1e-30)),
-            "finite": bool(torch.isfinite(got.float()).all())}
+            "max_abs_over_bf16": float(dq.max()) if d.numel() else 0.0,
+            "mean_rel": float(d.sum() / r.abs().sum().clamp_min(1e-30)),
+            "finite": bool(torch.isfinite(g).all())}
+
+
+def routing_agreement(got_idx: torch.Tensor, ref_idx: torch.Tensor, probs: torch.Tensor) -> dict:
+    """Rows whose top-k expert SET differs, and the oracle's relative gap
+    between its k-th and (k+1)-th probability on those rows."""
+    k = ref_idx.shape[-1]
+    g = torch.sort(got_idx.long(), dim=-1).values
+    r = torch.sort(ref_idx.long(), dim=-1).values
+    diff = (g != r).any(dim=-1)
+    vals, _ = canonical_topk(probs, min(k + 1, probs.shape[-1]))
+    if vals.shape[-1] > k:
+        gap = (vals[..., k - 1] - vals[..., k]) / vals[..., k - 1]
+    else:
+        gap = torch.zeros(vals.shape[:-1])
+    return {"rows": int(diff.numel()), "flipped": int(diff.sum()),
+            "max_flipped_gap": float(gap[diff].max()) if bool(diff.any()) else 0.0,
+            "flipped_mask": diff}
 
 
 __all__ = [n for n in dir() if not n.startswith("_") and n not in ("math", "np", "torch", "F")]

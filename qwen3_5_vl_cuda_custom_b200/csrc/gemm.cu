@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   else
     total = s_toff[p.E] * p.n_tiles;
 
-  const int k_blocks = p.K / kBK;
+  const int k_blocks = (p.K + kBK - 1) / kBK;  // TMA zero-fills the K tail
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------ TMA producer
@@ -358,8 +358,8 @@ extern "C" int q35_gemm_bf16(const void *a, const void *b, const void *bias,
                              int64_t N, int64_t K, q35_stream_t stream) {
   if (!a || !b || !out) return fail(Q35_ERR_INVALID, "gemm: null pointer");
   if (M < 0 || N <= 0 || K <= 0) return fail(Q35_ERR_SHAPE, "gemm: bad shape");
-  if (K % kBK != 0 || N % 32 != 0)
-    return fail(Q35_ERR_SHAPE, "gemm: K %lld must be x64 and N %lld x32",
+  if (K % 8 != 0 || N % 32 != 0)
+    return fail(Q35_ERR_SHAPE, "gemm: K %lld must be x8 and N %lld x32",
                 (long long)K, (long long)N);
   if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 24))
     return fail(Q35_ERR_SHAPE, "gemm: M/N too large");
@@ -412,8 +412,8 @@ static int grouped_common(const void *a, const void *w, void *out,
     return fail(Q35_ERR_SHAPE, "grouped_gemm: groups %d (1..%d)", E, kMaxGroups);
   if (rows_cap < 0 || rows_cap >= (int64_t(1) << 31))
     return fail(Q35_ERR_SHAPE, "grouped_gemm: rows_cap out of range");
-  if (K % kBK != 0 || N_out % 32 != 0)
-    return fail(Q35_ERR_SHAPE, "grouped_gemm: K %lld (x64) / N %lld (x32)",
+  if (K % 8 != 0 || N_out % 32 != 0)
+    return fail(Q35_ERR_SHAPE, "grouped_gemm: K %lld (x8) / N %lld (x32)",
                 (long long)K, (long long)N_out);
   if (!aligned16(out)) return fail(Q35_ERR_ALIGN, "grouped_gemm: out alignment");
   if (rows_cap == 0) return Q35_OK;

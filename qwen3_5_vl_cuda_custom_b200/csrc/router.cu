@@ -34,15 +34,15 @@ __device__ __forceinline__ void warp_argmax(float &v, int &i) {
   }
 }
 
-template <int EPT>  // experts per lane: E == 32 * EPT
+template <int EPT>  // experts per lane: E <= 32 * EPT
 __global__ void __launch_bounds__(256) router_kernel(
     const uint16_t *__restrict__ x, const float *__restrict__ wg,
     const float *__restrict__ bias, float *__restrict__ logits,
     int32_t *__restrict__ idx_out, float *__restrict__ w_out, int64_t T, int H,
-    int k, int renorm) {
-  constexpr int E = 32 * EPT;
+    int E, int k, int renorm) {
+  constexpr int EMAX = 32 * EPT;
   __shared__ float xs[kTokPerCta][kKc + 1];
-  __shared__ float ws[E][kKc + 1];
+  __shared__ float ws[EMAX][kKc + 1];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kTokPerCta;
@@ -71,10 +71,11 @@ __global__ void __launch_bounds__(256) router_kernel(
       xs[r][c + 3] = a3;
     }
     // gate tile: E rows x 32 columns of fp32.
-    for (int q = threadIdx.x; q < E * (kKc / 4); q += 256) {
+    for (int q = threadIdx.x; q < EMAX * (kKc / 4); q += 256) {
       const int e = q / (kKc / 4), c = (q % (kKc / 4)) * 4;
-      const float4 f =
-          *reinterpret_cast<const float4 *>(wg + static_cast<int64_t>(e) * H + h0 + c);
+      const float4 f = e < E ? *reinterpret_cast<const float4 *>(
+                                   wg + static_cast<int64_t>(e) * H + h0 + c)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
       ws[e][c] = f.x;
       ws[e][c + 1] = f.y;
       ws[e][c + 2] = f.z;
@@ -103,8 +104,13 @@ __global__ void __launch_bounds__(256) router_kernel(
     float l[EPT];
 #pragma unroll
     for (int j = 0; j < EPT; ++j) {
-      l[j] = acc[i][j] + (bias ? bias[lane + 32 * j] : 0.f);
-      logits[t * E + lane + 32 * j] = l[j];
+      const int e = lane + 32 * j;
+      if (e < E) {
+        l[j] = acc[i][j] + (bias ? bias[e] : 0.f);
+        logits[t * E + e] = l[j];
+      } else {
+        l[j] = -INFINITY;  // padding expert: exp() == 0, never selected
+      }
     }
     float m = -FLT_MAX;
 #pragma unroll
@@ -118,7 +124,7 @@ __global__ void __launch_bounds__(256) router_kernel(
     }
     s = warp_sum(s);
 #pragma unroll
-    for (int j = 0; j < EPT; ++j) p[j] = p[j] / s;
+    for (int j = 0; j < EPT; ++j) p[j] = (lane + 32 * j < E) ? p[j] / s : -2.f;
 
     // k rounds of warp argmax; a taken entry is knocked out with -1 (p >= 0).
     float sel_v = 0.f, tot = 0.f;
@@ -214,8 +220,8 @@ extern "C" int q35_router_topk_fwd(const void *x, const float *wg,
   if (T < 0 || H <= 0 || H % kKc != 0)
     return fail(Q35_ERR_SHAPE, "router: hidden %d must be a multiple of %d", H,
                 kKc);
-  if (E % 32 != 0 || E < 32 || E > 256)
-    return fail(Q35_ERR_UNSUPPORTED, "router: num_experts %d (32..256, x32)", E);
+  if (E < 1 || E > 256)
+    return fail(Q35_ERR_UNSUPPORTED, "router: num_experts %d (1..256)", E);
   if (k < 1 || k > 16 || k > E)
     return fail(Q35_ERR_SHAPE, "router: top_k %d (1..16, <= E)", k);
   if (!aligned16(wg) || !aligned16(x))
@@ -227,9 +233,9 @@ extern "C" int q35_router_topk_fwd(const void *x, const float *wg,
 #define Q35_ROUTER_CASE(EPT)                                              \
   case EPT:                                                               \
     router_kernel<EPT><<<grid, 256, 0, s>>>(xp, wg, bias, logits, idx,    \
-                                            weights, T, H, k, renorm);    \
+                                            weights, T, H, E, k, renorm);    \
     break;
-  switch (E / 32) {
+  switch ((E + 31) / 32) {
     Q35_ROUTER_CASE(1)
     Q35_ROUTER_CASE(2)
     Q35_ROUTER_CASE(3)

@@ -73,7 +73,7 @@ def multimodal_positions(B: int, S: int, img_off: int = 64, grid: int = 16) -> t
     """Config-5 positions: grid*grid image tokens at ``img_off`` with t = start,
     h = start + row, w = start + col; text after the image resumes at
     start + grid on all three axes."""
-    n_img = grid * grid
+    n_img = max(0, min(grid * grid, S - img_off))
     t = torch.arange(S, dtype=torch.int64)
     h = t.clone()
     w = t.clone()

@@ -40,10 +40,40 @@ def rotary(cfg, interleaved=False):
 
 
 def check(got, ref, what):
+    """bf16 output vs fp32 oracle: max-abs beyond the output's own bf16
+    rounding <= 2e-2 and mean relative error <= 5e-3."""
     s = O.error_stats(got.float().cpu(), ref)
     assert s["finite"], what
-    assert s["max_abs"] <= MAX_ABS and s["mean_rel"] <= MEAN_REL, (what, s)
+    assert s["max_abs_over_bf16"] <= MAX_ABS and s["mean_rel"] <= MEAN_REL, (what, s)
     return s
+
+
+def gpu_routing(layer, h_gpu, cfg):
+    m_in = layer.post_attention_layernorm(h_gpu).reshape(-1, cfg.hidden_size)
+    return layer.mlp.route(m_in)[1].cpu()
+
+
+MAX_FLIP_FRACTION = 0.03
+MAX_FLIP_GAP = 2e-2
+
+
+def check_layer_output(y, ref, gidx, cfg, recompute, what="layer output"):
+    """Layer output parity.  The top-k choice is a discrete function of the
+    MoE input, which the bf16 pipeline rounds (relative 2^-9) where the fp32
+    oracle does not, so tokens whose k-th and (k+1)-th expert probabilities
+    are within ~1% may pick the other one: (1) such disagreements are rare
+    (<= 3% of tokens) and only on near ties (oracle gap < 2%); (2) on tokens
+    whose expert set agrees the output meets the tolerance; (3) the oracle
+    re-run with the GPU's expert choice matches on every token."""
+    H = cfg.hidden_size
+    agree = O.routing_agreement(gidx, ref["top_idx"], ref["probs"])
+    assert agree["flipped"] <= max(2, int(agree["rows"] * MAX_FLIP_FRACTION)), (what, agree)
+    assert agree["max_flipped_gap"] < MAX_FLIP_GAP, (what, agree)
+    ok = ~agree["flipped_mask"]
+    check(y.reshape(-1, H)[ok.to(y.device)], ref["out"].reshape(-1, H)[ok], what + " (same experts)")
+    forced = recompute(gidx)
+    check(y, forced["out"], what + " (oracle with the GPU's expert choice)")
+    return agree
 
 
 def check_routing(layer, h_gpu, cfg, bias=None):
@@ -76,9 +106,11 @@ def run_prefill(cfg, seed, B, S, pos, x=None, norm_mode="unit", interleaved=Fals
     with torch.no_grad():
         y, rl, (k, v) = layer(xd, rot.bind(posd))
         h = layer.self_attn(layer.input_layernorm(xd), rot.bind(posd), residual=xd)[0]
+        gidx = gpu_routing(layer, h, cfg)
     ref = O.decoder_layer(x, P, cfg, pos, interleaved=interleaved)
     check(h, ref["h_attn"], "attention + residual")
-    check(y, ref["out"], "layer output")
+    check_layer_output(y, ref, gidx, cfg,
+                       lambda fi: O.decoder_layer(x, P, cfg, pos, interleaved=interleaved, force_idx=fi))
     check(k, ref["k"], "k cache")
     check(v, ref["v"], "v cache")
     assert rl.shape == (B * S, cfg.num_experts) and rl.dtype == torch.float32
@@ -97,10 +129,17 @@ def test_c1_tiny_layer_matches_reference_golden(golden):
         P = syn.layer_params(cfg, g, norm_mode=case["norm_mode"])
         x = syn.hidden_states((1, case["S"], cfg.hidden_size), g)
         layer = make_layer(cfg, P)
-        pos = syn.text_positions(1, case["S"]).to(DEV)
+        pos = syn.text_positions(1, case["S"])
+        xd = x.to(DEV, torch.bfloat16)
+        rb = rotary(cfg).bind(pos.to(DEV))
         with torch.no_grad():
-            y, rl, (k, v) = layer(x.to(DEV, torch.bfloat16), rotary(cfg).bind(pos))
-        check(y, case["out"], name)
+            y, rl, (k, v) = layer(xd, rb)
+            h = layer.self_attn(layer.input_layernorm(xd), rb, residual=xd)[0]
+            gidx = gpu_routing(layer, h, cfg)
+        ref = O.decoder_layer(x, P, cfg, pos)
+        ref["out"] = case["out"]  # the reference's own output
+        check_layer_output(y, ref, gidx, cfg,
+                           lambda fi: O.decoder_layer(x, P, cfg, pos, force_idx=fi), name)
         check(k, case["k"], name + " k")
 
 
@@ -132,10 +171,18 @@ def test_c1_multimodal_positions_golden(golden):
     P = syn.layer_params(cfg, g, norm_mode="unit")
     x = syn.hidden_states((1, case["S"], cfg.hidden_size), g)
     layer = make_layer(cfg, P)
-    pos = syn.multimodal_positions(1, case["S"], img_off=16, grid=8).to(DEV)
+    pos = syn.multimodal_positions(1, case["S"], img_off=16, grid=8)
+    xd = x.to(DEV, torch.bfloat16)
+    rb = rotary(cfg).bind(pos.to(DEV))
     with torch.no_grad():
-        y, _, _ = layer(x.to(DEV, torch.bfloat16), rotary(cfg).bind(pos))
-    check(y, case["out"], "multimodal")
+        y, _, (k, _) = layer(xd, rb)
+        h = layer.self_attn(layer.input_layernorm(xd), rb, residual=xd)[0]
+        gidx = gpu_routing(layer, h, cfg)
+    check(k, case["k"], "multimodal k (chunked mRoPE)")
+    ref = O.decoder_layer(x, P, cfg, pos)
+    ref["out"] = case["out"]
+    check_layer_output(y, ref, gidx, cfg, lambda fi: O.decoder_layer(x, P, cfg, pos, force_idx=fi),
+                       "multimodal")
 
 
 def test_c2_prefill_layer_full_size():

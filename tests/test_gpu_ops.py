@@ -166,7 +166,8 @@ def test_permutation_skewed_zipf():
 
 # ------------------------------------------------------------------ grouped GEMMs + combine
 @pytest.mark.parametrize("T,H,I,E,k", [(128, 256, 128, 16, 4), (1024, 2048, 768, 128, 8),
-                                       (37, 256, 64, 8, 2), (512, 512, 96, 32, 4)])
+                                       (37, 256, 64, 8, 2), (512, 512, 96, 32, 4),
+                                       (64, 256, 96, 4, 2)])
 def test_moe_experts_pipeline(T, H, I, E, k):
     g = gen(T * 3 + E)
     x = bf(torch.randn(T, H, generator=g))
@@ -250,7 +251,7 @@ def test_qknorm_mrope(D, sections, multimodal, interleaved):
 
 def test_mrope_op_matches_oracle():
     from qwen3_5_vl_cuda_custom_b200 import synthetic as syn
-    B, H, S, D = 2, 4, 300, 128
+    B, H, S, D = 2, 4, 400, 128
     x = bf(torch.randn(B, H, S, D))
     pos = syn.multimodal_positions(B, S)
     inv = O.inv_freq(D, 5e6)
