@@ -167,7 +167,7 @@ def staged_forward(layer, rot, x, pos, marks=None):
     mark("qknorm_mrope")
     o = K.attention_tokens(q, k, v, att.scale, True)
     mark("attention")
-    h = K.matmul(o, att.o_proj.weight, residual=x)
+    h = K.matmul(o, att.o_proj.weight, residual=x, out_dtype=torch.float32)
     mark("o_proj_residual")
     m_in = K.rmsnorm(h, layer.post_attention_layernorm.weight, layer.post_attention_layernorm.eps)
     mark("post_rmsnorm")

@@ -67,6 +67,14 @@ Q35_API const char *q35_version(void);
 Q35_API int q35_rmsnorm_fwd(const void *x, const void *w, void *y, int64_t rows,
                     int64_t cols, float eps, q35_stream_t stream);
 
+/* Same with fp32 input rows x [rows, cols] (the decoder layer keeps its
+ * post-attention residual stream in fp32); y bf16.  No separate reference
+ * entry: the reference normalises its bf16 residual (REF
+ * modules/text_decoder.py:59 -> csrc/rmsnorm_op.cu:8-60).                    */
+Q35_API int q35_rmsnorm_f32in_fwd(const float *x, const void *w, void *y,
+                                  int64_t rows, int64_t cols, float eps,
+                                  q35_stream_t stream);
+
 /* ---- QK-norm + mRoPE + head-major split ---------------------------------
  * Input qkv: bf16 [B*S, (Hq + 2*Hkv) * D], the fused q/k/v projection output
  * (token-major; columns q heads, then k heads, then v heads).
@@ -157,6 +165,14 @@ Q35_API int q35_gemm_bf16(const void *a, const void *b, const void *bias,
                   const void *residual, void *out, int64_t M, int64_t N,
                   int64_t K, q35_stream_t stream);
 
+/* Same GEMM with an fp32 output: out[m,n] = acc + bias[n] + residual[m,n]
+ * stored as fp32 (residual bf16).  The decoder layer uses it for o_proj so the
+ * post-attention residual h = x + attn is rounded once, at the layer output
+ * (the reference rounds it to bf16: REF modules/text_decoder.py:58).          */
+Q35_API int q35_gemm_bf16_f32out(const void *a, const void *b, const void *bias,
+                                 const void *residual, float *out, int64_t M,
+                                 int64_t N, int64_t K, q35_stream_t stream);
+
 /* Grouped expert GEMMs over the permuted rows of q35_moe_permute.
  * Group e owns rows [offsets[e], offsets[e+1]) of a (rows sorted by expert).
  * gate_up: act[r, j] = bf16( silu(g) * u ), g = a[r,:].w[e, j, :],
@@ -178,13 +194,15 @@ Q35_API int q35_grouped_gemm_down(const void *act, const void *w_down, void *y,
 
 /* ---- Combine --------------------------------------------------------------
  * out[t,:] = bf16( residual[t,:] + sum_j weights[t,j] * y[slot_pos[t*k+j],:] )
- * summed in fp32 in slot order; residual may be NULL.  slot_pos < 0 marks a
+ * summed in fp32 in slot order; residual may be NULL, bf16 or (residual_f32)
+ * fp32.  slot_pos < 0 marks a
  * slot whose row lives on another rank (skipped).  Replaces the weighted
  * index_add_forward + residual_add_forward pair (REF modules/moe.py:82-83,
  * csrc/moe_routing_op.cpp:9-13, modules/text_decoder.py:64).                 */
 Q35_API int q35_moe_combine(const void *y, const float *weights,
-                    const int32_t *slot_pos, const void *residual, void *out,
-                    int64_t T, int k, int64_t H, q35_stream_t stream);
+                            const int32_t *slot_pos, const void *residual,
+                            int residual_f32, void *out, int64_t T, int k,
+                            int64_t H, q35_stream_t stream);
 
 /* target[index[r],:] += source[r,:] (bf16 or fp32 rows by dtype code:
  * 0 = fp32, 1 = bf16), replaces index_add_forward

@@ -41,8 +41,12 @@ _SIGS = {
                                                c_int, c_int64, c_int, c_int, c_void_p]),
     "q35_grouped_gemm_down": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                       c_int64, c_int, c_int, c_void_p]),
-    "q35_moe_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int,
-                                c_int64, c_void_p]),
+    "q35_moe_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int64,
+                                c_int, c_int64, c_void_p]),
+    "q35_rmsnorm_f32in_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float,
+                                      c_void_p]),
+    "q35_gemm_bf16_f32out": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                     c_int64, c_int64, c_void_p]),
     "q35_index_add": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,
                               c_void_p]),
     "q35_swiglu_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),

@@ -57,6 +57,7 @@ struct GemmParams {
   const uint16_t *residual;    // [rows, ldr] or nullptr
   int64_t ldr;
   int *err;
+  int out_f32;                 // PLAIN epilogue: store fp32 instead of bf16
 };
 
 template <int BN, int STAGES>
@@ -298,7 +299,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] = rv[i] + v[i];
             }
-            store32(p.out + row * p.ldo + col, v);
+            if (p.out_f32) {
+              float4 *o = reinterpret_cast<float4 *>(
+                  reinterpret_cast<float *>(p.out) + row * p.ldo + col);
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+            } else {
+              store32(p.out + row * p.ldo + col, v);
+            }
           }
         }
       } else {
@@ -353,9 +362,9 @@ int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb,
 
 using namespace q35;
 
-extern "C" int q35_gemm_bf16(const void *a, const void *b, const void *bias,
-                             const void *residual, void *out, int64_t M,
-                             int64_t N, int64_t K, q35_stream_t stream) {
+static int gemm_dense(const void *a, const void *b, const void *bias,
+                      const void *residual, void *out, int64_t M, int64_t N,
+                      int64_t K, int out_f32, q35_stream_t stream) {
   if (!a || !b || !out) return fail(Q35_ERR_INVALID, "gemm: null pointer");
   if (M < 0 || N <= 0 || K <= 0) return fail(Q35_ERR_SHAPE, "gemm: bad shape");
   if (K % 8 != 0 || N % 32 != 0)
@@ -395,10 +404,24 @@ extern "C" int q35_gemm_bf16(const void *a, const void *b, const void *bias,
   p.residual = static_cast<const uint16_t *>(residual);
   p.ldr = N;
   p.err = err;
+  p.out_f32 = out_f32;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int tiles = static_cast<int>(mt * p.n_tiles);
   if (BN == 256) return launch_gemm<256, EPI_PLAIN, 4>(ta, tb, p, tiles, s);
   return launch_gemm<128, EPI_PLAIN, 6>(ta, tb, p, tiles, s);
+}
+
+extern "C" int q35_gemm_bf16(const void *a, const void *b, const void *bias,
+                             const void *residual, void *out, int64_t M,
+                             int64_t N, int64_t K, q35_stream_t stream) {
+  return gemm_dense(a, b, bias, residual, out, M, N, K, 0, stream);
+}
+
+extern "C" int q35_gemm_bf16_f32out(const void *a, const void *b,
+                                    const void *bias, const void *residual,
+                                    float *out, int64_t M, int64_t N,
+                                    int64_t K, q35_stream_t stream) {
+  return gemm_dense(a, b, bias, residual, out, M, N, K, 1, stream);
 }
 
 static int grouped_common(const void *a, const void *w, void *out,

@@ -85,6 +85,36 @@ __global__ void __launch_bounds__(256) rmsnorm_any_kernel(
   }
 }
 
+// fp32 input rows (the layer's fp32 residual stream), bf16 output; the row
+// stays in registers as NV float4 pairs per lane when cols == NV * 256.
+__global__ void __launch_bounds__(256) rmsnorm_f32in_kernel(
+    const float *__restrict__ x, const uint16_t *__restrict__ w,
+    uint16_t *__restrict__ y, int64_t rows, int64_t cols, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float *xr = x + row * cols;
+  float ss = 0.f;
+  for (int64_t c = lane * 8; c < cols; c += 256) {
+    const float4 a = *reinterpret_cast<const float4 *>(xr + c);
+    const float4 b = *reinterpret_cast<const float4 *>(xr + c + 4);
+    ss = fmaf(a.x, a.x, ss); ss = fmaf(a.y, a.y, ss); ss = fmaf(a.z, a.z, ss); ss = fmaf(a.w, a.w, ss);
+    ss = fmaf(b.x, b.x, ss); ss = fmaf(b.y, b.y, ss); ss = fmaf(b.z, b.z, ss); ss = fmaf(b.w, b.w, ss);
+  }
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(cols) + eps);
+  uint16_t *yr = y + row * cols;
+  for (int64_t c = lane * 8; c < cols; c += 256) {
+    const float4 a = *reinterpret_cast<const float4 *>(xr + c);
+    const float4 b = *reinterpret_cast<const float4 *>(xr + c + 4);
+    float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w}, wv[8];
+    load8(w + c, wv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (v[j] * r) * wv[j];
+    store8(yr + c, v);
+  }
+}
+
 // Rotary angle table for one token: cos/sin of pos[axis(j)] * inv_freq[j] for
 // j < D/2.  axis(j) follows the reference's chunked section layout
 // (REF kernels/mrope.py:19-35: sections*2 chunks, chunk i from axis i % 3;
@@ -259,6 +289,23 @@ extern "C" int q35_rmsnorm_fwd(const void *x, const void *w, void *y,
       rmsnorm_any_kernel<<<grid, 256, 0, s>>>(xp, wp, yp, rows, cols, eps);
   }
   Q35_LAUNCH_CHECK("rmsnorm launch");
+  return Q35_OK;
+}
+
+extern "C" int q35_rmsnorm_f32in_fwd(const float *x, const void *w, void *y,
+                                     int64_t rows, int64_t cols, float eps,
+                                     q35_stream_t stream) {
+  if (!x || !w || !y) return fail(Q35_ERR_INVALID, "rmsnorm_f32in: null pointer");
+  if (rows < 0 || cols <= 0 || cols % 8 != 0)
+    return fail(Q35_ERR_SHAPE, "rmsnorm_f32in: cols %lld must be a positive multiple of 8",
+                (long long)cols);
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y))
+    return fail(Q35_ERR_ALIGN, "rmsnorm_f32in: pointers must be 16-byte aligned");
+  if (rows == 0) return Q35_OK;
+  rmsnorm_f32in_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0,
+                         reinterpret_cast<cudaStream_t>(stream)>>>(
+      x, static_cast<const uint16_t *>(w), static_cast<uint16_t *>(y), rows, cols, eps);
+  Q35_LAUNCH_CHECK("rmsnorm_f32in launch");
   return Q35_OK;
 }
 

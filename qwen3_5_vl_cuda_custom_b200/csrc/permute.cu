@@ -140,8 +140,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(
 // slot order, one rounding).  One CTA per token, 8 columns per thread-step.
 __global__ void __launch_bounds__(256) combine_kernel(
     const uint16_t *__restrict__ y, const float *__restrict__ w,
-    const int32_t *__restrict__ slot_pos, const uint16_t *__restrict__ residual,
-    uint16_t *__restrict__ out, int k, int64_t H) {
+    const int32_t *__restrict__ slot_pos, const void *__restrict__ residual,
+    int residual_f32, uint16_t *__restrict__ out, int k, int64_t H) {
   const int64_t t = blockIdx.x;
   __shared__ int32_t s_pos[16];
   __shared__ float s_w[16];
@@ -169,12 +169,21 @@ __global__ void __launch_bounds__(256) combine_kernel(
       for (int q = 0; q < 8; ++q) acc[q] = fmaf(wj, v[q], acc[q]);
     }
     if (residual) {
-      const uint4 u = *reinterpret_cast<const uint4 *>(residual + t * H + c);
       float v[8];
-      unpack_bf2(u.x, v[0], v[1]);
-      unpack_bf2(u.y, v[2], v[3]);
-      unpack_bf2(u.z, v[4], v[5]);
-      unpack_bf2(u.w, v[6], v[7]);
+      if (residual_f32) {
+        const float *rp = static_cast<const float *>(residual) + t * H + c;
+        const float4 a = *reinterpret_cast<const float4 *>(rp);
+        const float4 b = *reinterpret_cast<const float4 *>(rp + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      } else {
+        const uint4 u = *reinterpret_cast<const uint4 *>(
+            static_cast<const uint16_t *>(residual) + t * H + c);
+        unpack_bf2(u.x, v[0], v[1]);
+        unpack_bf2(u.y, v[2], v[3]);
+        unpack_bf2(u.z, v[4], v[5]);
+        unpack_bf2(u.w, v[6], v[7]);
+      }
 #pragma unroll
       for (int q = 0; q < 8; ++q) acc[q] = v[q] + acc[q];
     }
@@ -298,8 +307,8 @@ extern "C" int q35_gather_rows(const void *src, const int32_t *rows, void *dst,
 
 extern "C" int q35_moe_combine(const void *y, const float *weights,
                                const int32_t *slot_pos, const void *residual,
-                               void *out, int64_t T, int k, int64_t H,
-                               q35_stream_t stream) {
+                               int residual_f32, void *out, int64_t T, int k,
+                               int64_t H, q35_stream_t stream) {
   if (!out || (T > 0 && (!y || !weights || !slot_pos)))
     return fail(Q35_ERR_INVALID, "moe_combine: null pointer");
   if (T < 0 || k < 1 || k > 16 || H <= 0 || H % 8 != 0)
@@ -310,9 +319,8 @@ extern "C" int q35_moe_combine(const void *y, const float *weights,
   if (T == 0) return Q35_OK;
   combine_kernel<<<static_cast<unsigned>(T), 256, 0,
                    reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t *>(y), weights, slot_pos,
-      static_cast<const uint16_t *>(residual), static_cast<uint16_t *>(out), k,
-      H);
+      static_cast<const uint16_t *>(y), weights, slot_pos, residual,
+      residual_f32, static_cast<uint16_t *>(out), k, H);
   Q35_LAUNCH_CHECK("moe_combine launch");
   return Q35_OK;
 }

@@ -43,22 +43,24 @@ def _require(t: torch.Tensor, name: str, dtype: torch.dtype | tuple = _BF16) -> 
 
 # ---------------------------------------------------------------- norms
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
-    """RMSNorm over the last dim (REF kernels/rmsnorm.py:66-77). bf16 only."""
-    x = _require(x, "rmsnorm.x")
-    weight = _require(weight.to(x.dtype) if weight.dtype != x.dtype else weight, "rmsnorm.weight")
+    """RMSNorm over the last dim (REF kernels/rmsnorm.py:66-77).  x bf16 (or
+    fp32: the layer's fp32 residual stream), weight bf16, output bf16."""
+    x = _require(x, "rmsnorm.x", (_BF16, torch.float32))
+    weight = _require(weight.to(_BF16) if weight.dtype != _BF16 else weight, "rmsnorm.weight")
     cols = x.shape[-1]
     if weight.numel() != cols:
         raise RuntimeError(f"rmsnorm: weight has {weight.numel()} elements, x has {cols} columns")
-    y = torch.empty_like(x)
+    y = torch.empty(x.shape, device=x.device, dtype=_BF16)
+    name = "q35_rmsnorm_fwd" if x.dtype == _BF16 else "q35_rmsnorm_f32in_fwd"
     with torch.cuda.device(x.device):
-        _lib.call("q35_rmsnorm_fwd", x.data_ptr(), weight.data_ptr(), y.data_ptr(),
+        _lib.call(name, x.data_ptr(), weight.data_ptr(), y.data_ptr(),
                   x.numel() // cols if cols else 0, cols, float(eps), _stream(x))
     return y
 
 
 # ---------------------------------------------------------------- GEMM
 def matmul(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
-           residual: torch.Tensor | None = None) -> torch.Tensor:
+           residual: torch.Tensor | None = None, out_dtype: torch.dtype = _BF16) -> torch.Tensor:
     """y = x @ weight^T (+ bias) (+ residual), REF kernels/matmul.py:62-77.
 
     bf16 in and out, fp32 accumulation on tcgen05.  ``residual`` (same shape as
@@ -71,7 +73,9 @@ def matmul(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
     if Kw != K:
         raise RuntimeError(f"matmul: x has K={K}, weight has K={Kw}")
     M = x.numel() // K if K else 0
-    out = torch.empty(*x.shape[:-1], N, device=x.device, dtype=x.dtype)
+    if out_dtype not in (_BF16, torch.float32):
+        raise RuntimeError(f"matmul: out_dtype {out_dtype} unsupported")
+    out = torch.empty(*x.shape[:-1], N, device=x.device, dtype=out_dtype)
     if bias is not None:
         bias = _require(bias, "matmul.bias")
     if residual is not None:
@@ -79,7 +83,8 @@ def matmul(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
         if residual.shape != out.shape:
             raise RuntimeError("matmul: residual shape must equal the output shape")
     with torch.cuda.device(x.device):
-        _lib.call("q35_gemm_bf16", x.data_ptr(), weight.data_ptr(), _ptr(bias), _ptr(residual),
+        _lib.call("q35_gemm_bf16" if out_dtype == _BF16 else "q35_gemm_bf16_f32out",
+                  x.data_ptr(), weight.data_ptr(), _ptr(bias), _ptr(residual),
                   out.data_ptr(), M, N, K, _stream(x))
     return out
 
@@ -246,11 +251,12 @@ def moe_combine(y: torch.Tensor, weights: torch.Tensor, slot_pos: torch.Tensor,
     slot_pos = _require(slot_pos, "combine.slot_pos", torch.int32)
     k = weights.shape[-1]
     if residual is not None:
-        residual = _require(residual, "combine.residual")
+        residual = _require(residual, "combine.residual", (_BF16, torch.float32))
+    r32 = 1 if residual is not None and residual.dtype == torch.float32 else 0
     out = torch.empty(T, H, device=weights.device, dtype=_BF16)
     with torch.cuda.device(weights.device):
         _lib.call("q35_moe_combine", y.data_ptr(), weights.data_ptr(), slot_pos.data_ptr(),
-                  _ptr(residual), out.data_ptr(), T, k, H, _stream(weights))
+                  _ptr(residual), r32, out.data_ptr(), T, k, H, _stream(weights))
     return out
 
 

@@ -65,8 +65,9 @@ class CudaLinear(nn.Module):
             bound = 1.0 / math.sqrt(fan_in) if fan_in > 0 else 0.0
             nn.init.uniform_(self.bias, -bound, bound)
 
-    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
-        return K.matmul(x, self.weight, self.bias, residual=residual)
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None,
+                out_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+        return K.matmul(x, self.weight, self.bias, residual=residual, out_dtype=out_dtype)
 
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, bias={self.bias is not None}"
@@ -241,9 +242,10 @@ class CudaFullAttention(nn.Module):
         return q.contiguous(), k.contiguous(), v.transpose(1, 2).contiguous()
 
     def forward(self, x: torch.Tensor, mrope_apply, past_kv: tuple[torch.Tensor, torch.Tensor] | None = None,
-                residual: torch.Tensor | None = None):
+                residual: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16):
         """``residual`` (optional, same shape as x) is added in the o_proj
-        epilogue; the decoder layer uses it to fuse its residual add."""
+        epilogue and ``out_dtype`` may be fp32: the decoder layer uses both to
+        fuse its residual add and keep the post-attention residual in fp32."""
         B, S, _ = x.shape
         q, k, v = self._project(x, mrope_apply)
         if past_kv is not None:
@@ -257,7 +259,7 @@ class CudaFullAttention(nn.Module):
         else:
             causal = S > 1
         out = K.attention_tokens(q, k, v, self.scale, causal)
-        return self.o_proj(out, residual=residual), new_kv
+        return self.o_proj(out, residual=residual, out_dtype=out_dtype), new_kv
 
 
 # ------------------------------------------------------------------ MoE
@@ -336,7 +338,9 @@ class CudaSparseMoE(nn.Module):
 class CudaTextDecoderLayer(nn.Module):
     """Pre-norm attention + residual, pre-norm MoE (or dense MLP) + residual
     (REF modules/text_decoder.py:14-65).  Both residual adds are fused into
-    the producing kernels (o_proj epilogue, MoE combine)."""
+    the producing kernels (o_proj epilogue, MoE combine), and the
+    post-attention residual h = x + attn stays fp32 between them, so the
+    layer output is rounded to bf16 once (the reference rounds h too)."""
 
     def __init__(self, hidden_size: int, num_heads: int, num_kv_heads: int, head_dim: int,
                  intermediate_size: int, rms_norm_eps: float, use_moe: bool = False,
@@ -357,10 +361,11 @@ class CudaTextDecoderLayer(nn.Module):
 
     def forward(self, x: torch.Tensor, mrope_apply, past_kv: tuple[torch.Tensor, torch.Tensor] | None = None):
         x = x.contiguous()
-        x, new_kv = self.self_attn(self.input_layernorm(x), mrope_apply, past_kv=past_kv, residual=x)
-        mlp_in = self.post_attention_layernorm(x)
+        h, new_kv = self.self_attn(self.input_layernorm(x), mrope_apply, past_kv=past_kv,
+                                   residual=x, out_dtype=torch.float32)
+        mlp_in = self.post_attention_layernorm(h)
         if self.use_moe:
-            x, router_logits = self.mlp(mlp_in, residual=x)
+            x, router_logits = self.mlp(mlp_in, residual=h)
         else:
-            x, router_logits = self.mlp(mlp_in, residual=x), None
+            x, router_logits = self.mlp(mlp_in, residual=h.to(torch.bfloat16)), None
         return x, router_logits, new_kv

@@ -105,7 +105,7 @@ def run_prefill(cfg, seed, B, S, pos, x=None, norm_mode="unit", interleaved=Fals
     posd = pos.to(DEV)
     with torch.no_grad():
         y, rl, (k, v) = layer(xd, rot.bind(posd))
-        h = layer.self_attn(layer.input_layernorm(xd), rot.bind(posd), residual=xd)[0]
+        h = layer.self_attn(layer.input_layernorm(xd), rot.bind(posd), residual=xd, out_dtype=torch.float32)[0]
         gidx = gpu_routing(layer, h, cfg)
     ref = O.decoder_layer(x, P, cfg, pos, interleaved=interleaved)
     check(h, ref["h_attn"], "attention + residual")
@@ -134,7 +134,7 @@ def test_c1_tiny_layer_matches_reference_golden(golden):
         rb = rotary(cfg).bind(pos.to(DEV))
         with torch.no_grad():
             y, rl, (k, v) = layer(xd, rb)
-            h = layer.self_attn(layer.input_layernorm(xd), rb, residual=xd)[0]
+            h = layer.self_attn(layer.input_layernorm(xd), rb, residual=xd, out_dtype=torch.float32)[0]
             gidx = gpu_routing(layer, h, cfg)
         ref = O.decoder_layer(x, P, cfg, pos)
         ref["out"] = case["out"]  # the reference's own output
@@ -176,7 +176,7 @@ def test_c1_multimodal_positions_golden(golden):
     rb = rotary(cfg).bind(pos.to(DEV))
     with torch.no_grad():
         y, _, (k, _) = layer(xd, rb)
-        h = layer.self_attn(layer.input_layernorm(xd), rb, residual=xd)[0]
+        h = layer.self_attn(layer.input_layernorm(xd), rb, residual=xd, out_dtype=torch.float32)[0]
         gidx = gpu_routing(layer, h, cfg)
     check(k, case["k"], "multimodal k (chunked mRoPE)")
     ref = O.decoder_layer(x, P, cfg, pos)

@@ -316,3 +316,20 @@ def test_flash_attention_reference_cases():
             q.float(), k_exp.float(), v_exp.float(), is_causal=causal, scale=scale)
         actual = K().flash_attention(q, k, v, scale=scale, is_causal=causal, num_kv_groups=4)
         torch.testing.assert_close(actual.float(), expected, atol=2e-2, rtol=2e-2)
+
+
+def test_fp32_residual_stream_ops():
+    """o_proj GEMM with fp32 output and the fp32-input RMSNorm the layer uses
+    to keep h = x + attn unrounded."""
+    g = gen(11)
+    a = bf(torch.randn(300, 512, generator=g))
+    b = bf(torch.randn(256, 512, generator=g) * 0.05)
+    res = bf(torch.randn(300, 256, generator=g))
+    out = K().matmul(a.to(DEV), b.to(DEV), residual=res.to(DEV), out_dtype=torch.float32)
+    assert out.dtype == torch.float32
+    ref = a.float() @ b.float().t() + res.float()
+    assert (out.cpu() - ref).abs().max() <= 2e-3 * ref.abs().max()
+    w = bf(1 + 0.02 * torch.randn(256, generator=g))
+    y = K().rmsnorm(out, w.to(DEV), 1e-6).float().cpu()
+    r = O.rmsnorm(out.cpu(), w.float(), 1e-6)
+    assert (y - r).abs().max() <= 2 ** -7 * r.abs().max() + 1e-6
