@@ -149,6 +149,26 @@ Q35_API int q35_moe_permute(const int32_t *idx, int64_t T, int k, int E,
                     int32_t *slot_pos, int32_t *tile_offsets,
                     int32_t *workspace, q35_stream_t stream);
 
+/* Allocation-free q35_moe_permute.  No counterpart in the reference: it is
+ * for callers that cannot allocate device memory while routing (a fixed
+ * memory pool that must not grow, a serving path where cudaMalloc is
+ * forbidden, a host that only passes input and output buffers).  Same inputs
+ * and outputs as q35_moe_permute minus `workspace`: the scratch is a 256 KiB
+ * array built into the library, held by every GPU that loads it until exit.
+ * Limit: ceil(T/128) * E <= q35_moe_permute_noalloc_max_workspace() (65536,
+ * e.g. T = 65536 tokens at E = 128); larger calls return Q35_ERR_SHAPE.
+ * The first call on a device looks up the array's device address (once per
+ * device); make that first call before any stream capture.  All calls share
+ * the one array: calls that overlap on the GPU (other streams, other host
+ * threads) race and must be serialised by the caller.  Out-of-range expert
+ * ids are dropped (slot_pos = -1) but not reported in the device error word.
+ * The call itself allocates nothing.                                        */
+Q35_API int64_t q35_moe_permute_noalloc_max_workspace(void);
+Q35_API int q35_moe_permute_noalloc(const int32_t *idx, int64_t T, int k, int E,
+                                    int32_t *counts, int32_t *offsets,
+                                    int32_t *sorted_tok, int32_t *slot_pos,
+                                    int32_t *tile_offsets, q35_stream_t stream);
+
 /* dst[r,:] = src[rows[r],:] for r < n (bf16, cols % 8 == 0); n may be read
  * from device memory (n_dev != NULL: *n_dev rows, at most n_max).           */
 Q35_API int q35_gather_rows(const void *src, const int32_t *rows, void *dst,

@@ -15,6 +15,8 @@
 //               popcount(mask[e] & bits below t); pos = offsets[e] +
 //               chunk_base[c][e] + rank.
 // Every step is integer arithmetic, so the result is bit-exact.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace q35 {
@@ -371,5 +373,92 @@ extern "C" int q35_residual_add_fwd(const void *a, const void *b, void *out,
       static_cast<const uint16_t *>(a), static_cast<const uint16_t *>(b),
       static_cast<uint16_t *>(out), n);
   Q35_LAUNCH_CHECK("residual_add launch");
+  return Q35_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of q35_moe_permute.
+//
+// Some callers cannot allocate device memory at the point where they route
+// tokens: code running inside a pre-sized memory pool that must not grow,
+// engines that forbid cudaMalloc on their serving path, or a host that only
+// hands out input and output buffers.  For them the per-chunk count scratch
+// that q35_moe_permute takes as `workspace` lives in the fixed array below.
+// The array is loaded with the library, so every GPU that loads it holds
+// 256 KiB until the process exits.
+namespace {
+constexpr int64_t kNoAllocScratchInts = 65536;  // 256 KiB of int32
+static __device__ __align__(256) int32_t g_permute_scratch[kNoAllocScratchInts];
+
+std::mutex g_scratch_mu;
+int32_t *g_scratch_ptr[64] = {};
+
+// Device address of g_permute_scratch on the current device, looked up once
+// per device.  The symbol's name in host code is only a host-side handle,
+// never a device pointer, so kernels get the address from here.
+int scratch_address(int32_t **out) {
+  int dev = 0;
+  Q35_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64)
+    return fail(Q35_ERR_NO_DEVICE, "moe_permute_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_permute_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_permute_scratch)");
+    g_scratch_ptr[dev] = static_cast<int32_t *>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return Q35_OK;
+}
+}  // namespace
+
+extern "C" int64_t q35_moe_permute_noalloc_max_workspace(void) {
+  return kNoAllocScratchInts;
+}
+
+extern "C" int q35_moe_permute_noalloc(const int32_t *idx, int64_t T, int k,
+                                       int E, int32_t *counts,
+                                       int32_t *offsets, int32_t *sorted_tok,
+                                       int32_t *slot_pos,
+                                       int32_t *tile_offsets,
+                                       q35_stream_t stream) {
+  if (!counts || !offsets || !tile_offsets ||
+      (T > 0 && (!idx || !sorted_tok || !slot_pos)))
+    return fail(Q35_ERR_INVALID, "moe_permute_noalloc: null pointer");
+  if (T < 0 || k < 1 || E < 1 || E > 1024)
+    return fail(Q35_ERR_SHAPE, "moe_permute_noalloc: T %lld k %d E %d (E <= 1024)",
+                (long long)T, k, E);
+  if (T * k >= (int64_t(1) << 31))
+    return fail(Q35_ERR_SHAPE, "moe_permute_noalloc: T*k exceeds int32");
+  const int64_t need = q35_moe_permute_workspace(T, E);
+  if (need > kNoAllocScratchInts)
+    return fail(Q35_ERR_SHAPE,
+                "moe_permute_noalloc: needs %lld scratch ints (ceil(T/128)*E), the "
+                "built-in maximum is %lld; use q35_moe_permute with a caller workspace",
+                (long long)need, (long long)kNoAllocScratchInts);
+  int32_t *scratch = nullptr;
+  const int st = scratch_address(&scratch);
+  if (st) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t chunks = (T + kChunk - 1) / kChunk;
+  const size_t smem = static_cast<size_t>(E) * 4 * sizeof(uint32_t);
+  // The count pass writes every scratch entry the scan and scatter read, so
+  // nothing left over from a previous call is ever used.  Expert ids outside
+  // [0, E) are dropped (slot_pos = -1) without a device error-word report:
+  // that word is allocated on first use, which this entry point must not do.
+  if (chunks > 0) {
+    permute_count_kernel<<<static_cast<unsigned>(chunks), kChunk, smem, s>>>(
+        idx, T, k, E, scratch, nullptr);
+    Q35_LAUNCH_CHECK("permute_noalloc count launch");
+  }
+  permute_scan_kernel<<<1, 1024, 0, s>>>(scratch, chunks, E, counts, offsets,
+                                         tile_offsets);
+  Q35_LAUNCH_CHECK("permute_noalloc scan launch");
+  if (chunks > 0) {
+    permute_scatter_kernel<<<static_cast<unsigned>(chunks), kChunk, smem, s>>>(
+        idx, T, k, E, scratch, offsets, sorted_tok, slot_pos, nullptr);
+    Q35_LAUNCH_CHECK("permute_noalloc scatter launch");
+  }
   return Q35_OK;
 }
