@@ -111,12 +111,29 @@ Q35_API int q35_mrope_fwd(const void *x, void *y, const int64_t *positions,
  * Replaces the router of CudaSparseMoE.forward (REF modules/moe.py:60-65):
  *   matmul_forward (csrc/matmul_op.cpp:11-14) -> softmax_forward
  *   (csrc/softmax_op.cpp:6-9) -> topk_forward (csrc/moe_routing_op.cpp:9-13).
- * bias may be NULL.  1 <= E <= 256, k <= 16, H % 32 == 0.
+ * bias and wg_split may be NULL.  1 <= E <= 256, k <= 16, H % 32 == 0.
  * idx is int32 (the reference returns int64; values are equal).            */
-Q35_API int q35_router_topk_fwd(const void *x, const float *wg, const float *bias,
-                        float *logits, int32_t *idx, float *weights,
-                        int64_t T, int H, int E, int k, int renorm,
-                        q35_stream_t stream);
+Q35_API int q35_router_topk_fwd(const void *x, const float *wg, const void *wg_split,
+                                const float *bias, float *logits, int32_t *idx,
+                                float *weights, int64_t T, int H, int E, int k,
+                                int renorm, float *workspace, q35_stream_t stream);
+/* fp32 elements of `workspace` the tensor-core path needs (wg_split != NULL). */
+Q35_API int64_t q35_router_workspace(int64_t T, int H, int E);
+
+/* Tensor-core router inputs.  q35_router_split_weights writes w3 (bf16
+ * [E, 3H]) = [lo | mid | hi] with lo + mid + hi == wg exactly (8 significant
+ * bits each); passing it as wg_split above (H % 64 == 0, E % 32 == 0) computes
+ * the logits as a tcgen05 GEMM of [x | x | x] against w3 -- every product is
+ * exact in fp32 and accumulates in fp32 in k_splits partial sums -- instead of
+ * the fp32 SIMT GEMV.  q35_router_logits_tc is that GEMM alone, writing
+ * partial planes fp32 [k_splits, T, E] (k_splits must divide 3H/64).  No
+ * reference counterpart (the reference computes the logits with its SIMT
+ * matmul_fwd_kernel, REF csrc/matmul_op.cu:15-92).                           */
+Q35_API int q35_router_split_weights(const float *wg, void *w3, int E, int H,
+                                     q35_stream_t stream);
+Q35_API int q35_router_logits_tc(const void *x, const void *w3, float *partials,
+                                 int64_t T, int H, int E, int k_splits,
+                                 q35_stream_t stream);
 
 /* Row softmax in fp32, replaces softmax_forward (REF csrc/softmax_op.cpp:6-9).
  * x, y: fp32 [rows, cols], cols <= 4096.                                     */

@@ -28,7 +28,12 @@ _SIGS = {
     "q35_mrope_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, _i32p, c_int, c_int64, c_int,
                               c_int64, c_int, c_void_p]),
     "q35_router_topk_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-                                    c_int64, c_int, c_int, c_int, c_int, c_void_p]),
+                                    c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p,
+                                    c_void_p]),
+    "q35_router_workspace": (c_int64, [c_int64, c_int, c_int]),
+    "q35_router_split_weights": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "q35_router_logits_tc": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int,
+                                     c_void_p]),
     "q35_softmax_fwd": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p]),
     "q35_topk_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_void_p]),
     "q35_moe_permute_workspace": (c_int64, [c_int64, c_int]),

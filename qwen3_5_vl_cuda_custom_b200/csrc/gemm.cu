@@ -58,6 +58,9 @@ struct GemmParams {
   int64_t ldr;
   int *err;
   int out_f32;                 // PLAIN epilogue: store fp32 instead of bf16
+  int a_k_wrap;                // > 0: A's K coordinate wraps at this width
+  int k_splits;                // dense only: K split into this many partial planes
+  int64_t split_stride;        // elements between partial output planes
 };
 
 template <int BN, int STAGES>
@@ -80,14 +83,19 @@ struct TileInfo {
   int rows_valid;  // rows of the tile that belong to the group
   int group;
   int nt;          // n-tile index
+  int split;       // K split (dense split-K), else 0
 };
 
 __device__ __forceinline__ TileInfo decode_tile(int tile, const GemmParams &p,
                                                 const int *s_off,
                                                 const int *s_toff) {
   TileInfo ti;
+  ti.split = 0;
   if (p.offsets == nullptr) {
     const int mtiles = (p.M + kBM - 1) / kBM;
+    const int per_split = mtiles * p.n_tiles;
+    ti.split = tile / per_split;
+    tile -= ti.split * per_split;
     ti.nt = tile / mtiles;
     const int mt = tile - ti.nt * mtiles;
     ti.group = 0;
@@ -191,11 +199,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   int total;
   if (p.offsets == nullptr)
-    total = ((p.M + kBM - 1) / kBM) * p.n_tiles;
+    total = ((p.M + kBM - 1) / kBM) * p.n_tiles * max(1, p.k_splits);
   else
     total = s_toff[p.E] * p.n_tiles;
 
   const int k_blocks = (p.K + kBK - 1) / kBK;  // TMA zero-fills the K tail
+  // Split-K: split s covers k-blocks [s * kb_per, (s + 1) * kb_per); the host
+  // only uses splits that divide k_blocks, so no split is empty.
+  const int kb_per = k_blocks / max(1, p.k_splits);
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------ TMA producer
@@ -204,7 +215,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
       const TileInfo ti = decode_tile(tile, p, s_off, s_toff);
       const int brow = ti.group * p.b_rows_per_group + ti.nt * p.b_tile_step;
-      for (int kb = 0; kb < k_blocks; ++kb, ++g) {
+      const int kb0 = ti.split * kb_per;
+      for (int kb = kb0; kb < kb0 + kb_per; ++kb, ++g) {
         const int s = g % STAGES;
         const uint32_t ph = (g / STAGES) & 1u;
         if (!sm100::mbar_wait(&empty[s], ph ^ 1u)) {
@@ -215,7 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t *sa = smem + s * L::kStageBytes;
         uint8_t *sb = sa + L::kABytes;
         sm100::mbar_arrive_expect_tx(&full[s], L::kStageBytes);
-        sm100::tma_load_2d(sa, &tmA, &full[s], kb * kBK, ti.row0);
+        const int ka = p.a_k_wrap ? (kb * kBK) % p.a_k_wrap : kb * kBK;
+        sm100::tma_load_2d(sa, &tmA, &full[s], ka, ti.row0);
         sm100::tma_load_2d(sb, &tmB, &full[s], kb * kBK, brow);
         sm100::tma_load_2d(sb + L::kBBytes / 2, &tmB, &full[s], kb * kBK,
                            brow + p.b_second_off);
@@ -234,7 +247,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       sm100::tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
-      for (int kb = 0; kb < k_blocks; ++kb, ++g) {
+      const int kb0 = decode_tile(tile, p, s_off, s_toff).split * kb_per;
+      for (int kb = kb0; kb < kb0 + kb_per; ++kb, ++g) {
         const int s = g % STAGES;
         const uint32_t ph = (g / STAGES) & 1u;
         if (!sm100::mbar_wait(&full[s], ph)) {
@@ -249,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk)
           sm100::mma_bf16_ss(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc,
-                             (kb | kk) != 0 ? 1u : 0u);
+                             (kb != kb0 || kk != 0) ? 1u : 0u);
         sm100::mma_commit(&empty[s]);
       }
       sm100::mma_commit(&tfull[acc]);
@@ -301,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             if (p.out_f32) {
               float4 *o = reinterpret_cast<float4 *>(
-                  reinterpret_cast<float *>(p.out) + row * p.ldo + col);
+                  reinterpret_cast<float *>(p.out) + ti.split * p.split_stride + row * p.ldo + col);
 #pragma unroll
               for (int q = 0; q < 8; ++q)
                 o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
@@ -422,6 +436,55 @@ extern "C" int q35_gemm_bf16_f32out(const void *a, const void *b,
                                     float *out, int64_t M, int64_t N,
                                     int64_t K, q35_stream_t stream) {
   return gemm_dense(a, b, bias, residual, out, M, N, K, 1, stream);
+}
+
+// Router logits on the tensor cores.  The fp32 gate weight is stored as three
+// bf16 planes w3[e] = [lo | mid | hi] with lo + mid + hi == w exactly (each
+// plane holds 8 significant bits), and x is bf16, so every product x*plane is
+// exact in fp32; logits = sum over the 3H columns of x3 * w3 with x3 = [x|x|x]
+// (A's K coordinate wraps at H instead of materialising x3).  The tensor
+// core's fp32 accumulation truncates relative to the running sum, so the
+// small planes are accumulated first and K is split into k_splits fresh
+// accumulators written as partial planes [k_splits, T, E]; the top-k kernel
+// adds them in a fixed order (deterministic).
+extern "C" int q35_router_logits_tc(const void *x, const void *w3,
+                                    float *partials, int64_t T, int H, int E,
+                                    int k_splits, q35_stream_t stream) {
+  if (!x || !w3 || !partials) return fail(Q35_ERR_INVALID, "router_logits_tc: null pointer");
+  if (k_splits < 1 || (3 * H / kBK) % k_splits != 0)
+    return fail(Q35_ERR_SHAPE, "router_logits_tc: %d splits must divide %d k-blocks", k_splits,
+                3 * H / kBK);
+  if (T < 0 || H <= 0 || H % kBK != 0 || E <= 0 || E % 32 != 0 || E > 4096)
+    return fail(Q35_ERR_SHAPE, "router_logits_tc: H %d (x64) E %d (x32)", H, E);
+  if (!aligned16(partials)) return fail(Q35_ERR_ALIGN, "router_logits_tc: output alignment");
+  if (T == 0) return Q35_OK;
+  int *err = device_error_word();
+  if (!err) return fail(Q35_ERR_CUDA, "router_logits_tc: no device error word");
+  constexpr int BN = 64;
+  CUtensorMap ta, tb;
+  int st = make_tmap_bf16_2d(&ta, x, H, T, static_cast<uint64_t>(H) * 2, kBK, kBM);
+  if (st) return st;
+  st = make_tmap_bf16_2d(&tb, w3, 3 * static_cast<uint64_t>(H), E,
+                         3 * static_cast<uint64_t>(H) * 2, kBK, BN / 2);
+  if (st) return st;
+  GemmParams p{};
+  p.M = static_cast<int>(T);
+  p.E = 1;
+  p.N = E;
+  p.K = 3 * H;
+  p.n_tiles = (E + BN - 1) / BN;
+  p.b_rows_per_group = E;
+  p.b_tile_step = BN;
+  p.b_second_off = BN / 2;
+  p.out = reinterpret_cast<uint16_t *>(partials);
+  p.ldo = E;
+  p.err = err;
+  p.out_f32 = 1;
+  p.a_k_wrap = H;
+  p.k_splits = k_splits;
+  p.split_stride = T * static_cast<int64_t>(E);
+  const int tiles = static_cast<int>(((T + kBM - 1) / kBM) * p.n_tiles * k_splits);
+  return launch_gemm<BN, EPI_PLAIN, 8>(ta, tb, p, tiles, reinterpret_cast<cudaStream_t>(stream));
 }
 
 static int grouped_common(const void *a, const void *w, void *out,

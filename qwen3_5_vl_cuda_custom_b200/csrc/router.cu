@@ -157,6 +157,96 @@ __global__ void __launch_bounds__(256) router_kernel(
   }
 }
 
+// Softmax + top-k + renormalise of the tensor-core router's logits: one warp
+// per token, lane l holds experts l, l+32, ...; the logits are the sum of the
+// split-K partial planes (+ bias), written to `logits`.
+template <int EPT>
+__global__ void __launch_bounds__(256) topk_from_logits_kernel(
+    const float *__restrict__ partials, int n_partials, float *__restrict__ logits,
+    const float *__restrict__ bias, int32_t *__restrict__ idx_out,
+    float *__restrict__ w_out, int64_t T, int E, int k, int renorm) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  float l[EPT];
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    const int e = lane + 32 * j;
+    if (e < E) {
+      // Partial K planes summed in a fixed order (deterministic).
+      float v = partials[t * E + e];
+      for (int q = 1; q < n_partials; ++q) v += partials[(q * T + t) * E + e];
+      if (bias) v += bias[e];
+      l[j] = v;
+      logits[t * E + e] = v;
+    } else {
+      l[j] = -INFINITY;
+    }
+  }
+  float m = -FLT_MAX;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) m = fmaxf(m, l[j]);
+  m = warp_max(m);
+  float p[EPT], s = 0.f;
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) {
+    p[j] = expf(l[j] - m);
+    s += p[j];
+  }
+  s = warp_sum(s);
+#pragma unroll
+  for (int j = 0; j < EPT; ++j) p[j] = (lane + 32 * j < E) ? p[j] / s : -2.f;
+  float sel_v = 0.f, tot = 0.f;
+  int sel_i = 0;
+  for (int r = 0; r < k; ++r) {
+    float bv = -1.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < EPT; ++j)
+      if (p[j] > bv) {
+        bv = p[j];
+        bi = lane + 32 * j;
+      }
+    warp_argmax(bv, bi);
+    if ((bi & 31) == lane) {
+#pragma unroll
+      for (int j = 0; j < EPT; ++j)
+        if (lane + 32 * j == bi) p[j] = -1.f;
+    }
+    if (lane == r) {
+      sel_v = bv;
+      sel_i = bi;
+    }
+    tot += bv;
+  }
+  if (lane < k) {
+    idx_out[t * k + lane] = sel_i;
+    w_out[t * k + lane] = renorm ? sel_v / tot : sel_v;
+  }
+}
+
+// w3[e] = [lo | mid | hi] bf16 planes with lo + mid + hi == w[e] exactly:
+// hi = rn(w), mid = rn(w - hi), lo = rn(w - hi - mid); each remainder is exact
+// in fp32 and each plane holds the next 8 significant bits of w's 24.  The
+// small planes come first so the tensor core accumulates them while the
+// running sum is still small.
+__global__ void split_weights_kernel(const float *__restrict__ wg,
+                                     uint16_t *__restrict__ w3, int E, int H) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<int64_t>(E) * H) return;
+  const int64_t e = i / H, h = i % H;
+  const float w = wg[i];
+  const uint16_t hi = f2bf(w);
+  const float r1 = w - bf2f(hi);
+  const uint16_t mid = f2bf(r1);
+  const float r2 = r1 - bf2f(mid);
+  const uint16_t lo = f2bf(r2);
+  uint16_t *row = w3 + e * 3 * static_cast<int64_t>(H);
+  row[h] = lo;
+  row[H + h] = mid;
+  row[2 * H + h] = hi;
+}
+
 // Standalone row softmax (fp32), one warp per row.
 __global__ void __launch_bounds__(256) softmax_kernel(const float *__restrict__ x,
                                                       float *__restrict__ y,
@@ -210,11 +300,35 @@ __global__ void __launch_bounds__(256) topk_kernel(const float *__restrict__ x,
 
 using namespace q35;
 
+extern "C" int q35_router_logits_tc(const void *x, const void *w3,
+                                    float *partials, int64_t T, int H, int E,
+                                    int k_splits, q35_stream_t stream);
+
+// Split-K factor of the tensor-core router: 4 fresh accumulators when the
+// 3H/64 k-blocks divide evenly, else 1.
+static int router_splits(int H) { return ((3 * H / 64) % 4 == 0) ? 4 : 1; }
+
+extern "C" int64_t q35_router_workspace(int64_t T, int H, int E) {
+  return static_cast<int64_t>(router_splits(H)) * T * E;
+}
+
+extern "C" int q35_router_split_weights(const float *wg, void *w3, int E,
+                                        int H, q35_stream_t stream) {
+  if (!wg || !w3) return fail(Q35_ERR_INVALID, "router_split_weights: null pointer");
+  if (E <= 0 || H <= 0) return fail(Q35_ERR_SHAPE, "router_split_weights: bad shape");
+  const int64_t n = static_cast<int64_t>(E) * H;
+  split_weights_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
+                         reinterpret_cast<cudaStream_t>(stream)>>>(
+      wg, static_cast<uint16_t *>(w3), E, H);
+  Q35_LAUNCH_CHECK("router_split_weights launch");
+  return Q35_OK;
+}
+
 extern "C" int q35_router_topk_fwd(const void *x, const float *wg,
-                                   const float *bias, float *logits,
-                                   int32_t *idx, float *weights, int64_t T,
-                                   int H, int E, int k, int renorm,
-                                   q35_stream_t stream) {
+                                   const void *wg_split, const float *bias,
+                                   float *logits, int32_t *idx, float *weights,
+                                   int64_t T, int H, int E, int k, int renorm,
+                                   float *workspace, q35_stream_t stream) {
   if (!x || !wg || !logits || !idx || !weights)
     return fail(Q35_ERR_INVALID, "router: null pointer");
   if (T < 0 || H <= 0 || H % kKc != 0)
@@ -228,6 +342,34 @@ extern "C" int q35_router_topk_fwd(const void *x, const float *wg,
     return fail(Q35_ERR_ALIGN, "router: x / gate weight not 16-byte aligned");
   if (T == 0) return Q35_OK;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (wg_split != nullptr && H % 64 == 0 && E % 32 == 0) {
+    // Tensor-core logits, then softmax / top-k on the fp32 logits.
+    if (!workspace)
+      return fail(Q35_ERR_INVALID, "router: the tensor-core path needs a workspace");
+    const int ns = router_splits(H);
+    int st = q35_router_logits_tc(x, wg_split, workspace, T, H, E, ns, stream);
+    if (st) return st;
+    const unsigned g2 = static_cast<unsigned>((T + 7) / 8);
+#define Q35_TOPK_CASE(EPT)                                                     \
+  case EPT:                                                                    \
+    topk_from_logits_kernel<EPT><<<g2, 256, 0, s>>>(workspace, ns, logits,    \
+                                                    bias, idx, weights, T, E, \
+                                                    k, renorm);                \
+    break;
+    switch ((E + 31) / 32) {
+      Q35_TOPK_CASE(1)
+      Q35_TOPK_CASE(2)
+      Q35_TOPK_CASE(3)
+      Q35_TOPK_CASE(4)
+      Q35_TOPK_CASE(5)
+      Q35_TOPK_CASE(6)
+      Q35_TOPK_CASE(7)
+      Q35_TOPK_CASE(8)
+    }
+#undef Q35_TOPK_CASE
+    Q35_LAUNCH_CHECK("router topk launch");
+    return Q35_OK;
+  }
   const unsigned grid = static_cast<unsigned>((T + kTokPerCta - 1) / kTokPerCta);
   auto xp = static_cast<const uint16_t *>(x);
 #define Q35_ROUTER_CASE(EPT)                                              \

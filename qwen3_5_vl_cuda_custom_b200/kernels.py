@@ -151,9 +151,21 @@ def residual_add(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def router_split_weights(gate_weight: torch.Tensor) -> torch.Tensor:
+    """bf16 [E, 3H] planes [hi | mid | lo] summing exactly to the fp32 gate weight."""
+    wg = _require(gate_weight, "router_split.gate_weight", torch.float32)
+    E, H = wg.shape
+    w3 = torch.empty(E, 3 * H, device=wg.device, dtype=_BF16)
+    with torch.cuda.device(wg.device):
+        _lib.call("q35_router_split_weights", wg.data_ptr(), w3.data_ptr(), E, H, _stream(wg))
+    return w3
+
+
 def router_topk(x2d: torch.Tensor, gate_weight: torch.Tensor, top_k: int, renorm: bool = True,
-                bias: torch.Tensor | None = None):
-    """Fused fp32 router: logits (T,E) fp32, top-k ids (T,k) int32, weights (T,k) fp32."""
+                bias: torch.Tensor | None = None, gate_split: torch.Tensor | None = None):
+    """Fused fp32 router: logits (T,E) fp32, top-k ids (T,k) int32, weights (T,k) fp32.
+    With ``gate_split`` (router_split_weights(gate_weight)) the logits run on the
+    tensor cores (exact bf16 products, fp32 accumulation)."""
     x2d = _require(x2d, "router.x")
     wg = _require(gate_weight, "router.gate_weight", torch.float32)
     T, H = x2d.shape
@@ -163,9 +175,15 @@ def router_topk(x2d: torch.Tensor, gate_weight: torch.Tensor, top_k: int, renorm
     w = torch.empty(T, top_k, device=x2d.device, dtype=torch.float32)
     if bias is not None:
         bias = _require(bias, "router.bias", torch.float32)
+    ws = None
+    if gate_split is not None:
+        gate_split = _require(gate_split, "router.gate_split")
+        ws = torch.empty(max(1, _lib.query("q35_router_workspace", T, H, E)), device=x2d.device,
+                         dtype=torch.float32)
     with torch.cuda.device(x2d.device):
-        _lib.call("q35_router_topk_fwd", x2d.data_ptr(), wg.data_ptr(), _ptr(bias), logits.data_ptr(),
-                  idx.data_ptr(), w.data_ptr(), T, H, E, int(top_k), 1 if renorm else 0, _stream(x2d))
+        _lib.call("q35_router_topk_fwd", x2d.data_ptr(), wg.data_ptr(), _ptr(gate_split), _ptr(bias),
+                  logits.data_ptr(), idx.data_ptr(), w.data_ptr(), T, H, E, int(top_k),
+                  1 if renorm else 0, _ptr(ws), _stream(x2d))
     return logits, idx, w
 
 

@@ -310,10 +310,24 @@ class CudaSparseMoE(nn.Module):
             self.router_bias = rb.to(device=new.device, dtype=torch.float32)
         return out
 
+    def _gate_split(self):
+        """bf16 [hi | mid | lo] planes of the fp32 gate weight for the tensor-core
+        router (rebuilt when the weight is replaced or modified in place)."""
+        H, E = self.hidden_size, self.num_experts
+        if H % 64 or E % 32:
+            return None
+        key = _params_key(self.gate_weight)
+        cache = getattr(self, "_split_cache", None)
+        if cache is None or cache[0] != key:
+            with torch.no_grad():
+                cache = (key, K.router_split_weights(self.gate_weight.detach()))
+            self._split_cache = cache
+        return cache[1]
+
     def route(self, x2d: torch.Tensor):
         """Router only: (logits fp32 (T,E), top-k ids int32 (T,k), weights fp32 (T,k))."""
         return K.router_topk(x2d, self.gate_weight, self.top_k, self.norm_topk_prob,
-                             bias=self.router_bias)
+                             bias=self.router_bias, gate_split=self._gate_split())
 
     def experts(self, x2d: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor,
                 residual: torch.Tensor | None = None) -> torch.Tensor:

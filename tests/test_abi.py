@@ -46,7 +46,7 @@ def test_null_pointer_rejected_before_launch(lib):
 def test_bad_shapes_rejected(lib):
     p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
     assert lib.q35_rmsnorm_fwd(p, p, p, 4, 250, 1e-6, None) == 2
-    assert lib.q35_router_topk_fwd(p, p, None, p, p, p, 4, 256, 300, 4, 1, None) == 4
+    assert lib.q35_router_topk_fwd(p, p, None, None, p, p, p, 4, 256, 300, 4, 1, None, None) == 4
     assert lib.q35_gemm_bf16(p, p, None, None, p, 16, 64, 100, None) == 2
     assert lib.q35_attn_prefill_fwd(p, p, p, p, None, 1, 8, 2, 16, 16, 48, 0.1, 1, None) == 4
     assert lib.q35_attn_decode_fwd(p, p, p, p, 1, 32, 1, 1, 16, 128, 0.1, p, None) == 2

@@ -96,6 +96,27 @@ def test_router(T, H, E, k):
     assert (w.cpu()[ok] - rw[ok]).abs().max() < 1e-5
 
 
+@pytest.mark.parametrize("T,H,E,k", [(4096, 2048, 128, 8), (77, 256, 32, 4), (300, 512, 256, 16),
+                                     (1, 2048, 128, 8)])
+def test_router_tensor_core_path(T, H, E, k):
+    """Logits from the exact bf16 split of the fp32 gate on tcgen05."""
+    g = gen(T * 5 + E)
+    x = bf(torch.randn(T, H, generator=g))
+    wg = torch.randn(E, H, generator=g) * 0.02
+    w3 = K().router_split_weights(wg.to(DEV))
+    parts = w3.view(E, 3, H).float().sum(1).cpu()
+    assert torch.equal(parts, wg), "lo + mid + hi must equal the fp32 weight exactly"
+    bias = torch.randn(E, generator=g) * 0.1
+    logits, idx, w = K().router_topk(x.to(DEV), wg.to(DEV), k, bias=bias.to(DEV), gate_split=w3)
+    rl, p, ridx, rw = O.router(x.float(), wg, k, bias=bias)
+    # the tensor core accumulates fp32 with truncation: logits agree to ~1e-5,
+    # so rows whose k-th / (k+1)-th probabilities are within 1e-4 may swap
+    assert (logits.cpu() - rl).abs().max() < 2e-5
+    ok = ~O.near_tie_rows(p, k, rel=1e-4)
+    assert torch.equal(idx.cpu().long()[ok], ridx[ok])
+    assert (w.cpu()[ok] - rw[ok]).abs().max() < 1e-5
+
+
 def test_router_ties_to_lower_index():
     """All-equal logits: every expert ties; the top-k must be 0..k-1."""
     x = torch.zeros(4, 256, dtype=torch.bfloat16, device=DEV)
