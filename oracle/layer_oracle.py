@@ -217,13 +217,15 @@ def decoder_layer(x: torch.Tensor, P: dict, cfg, position_ids, past_kv=None,
 
 
 def near_tie_rows(probs: torch.Tensor, k: int, rel: float = 1e-5) -> torch.Tensor:
-    """Rows whose k-th and (k+1)-th probabilities differ by less than rel * p_k:
-    an fp32 GEMV with another summation order may legitimately swap them."""
+    """Rows where two neighbours among the sorted top-(k+1) probabilities differ
+    by less than rel * the larger one: a logit computed in another summation
+    order may legitimately swap them (the set at the k-th/(k+1)-th boundary,
+    the order inside the top-k)."""
     vals, _ = canonical_topk(probs, min(k + 1, probs.shape[-1]))
-    if vals.shape[-1] <= k:
+    if vals.shape[-1] < 2:
         return torch.zeros(probs.shape[0], dtype=torch.bool)
-    gap = vals[..., k - 1] - vals[..., k]
-    return gap < rel * vals[..., k - 1]
+    gap = vals[..., :-1] - vals[..., 1:]
+    return (gap < rel * vals[..., :-1]).any(dim=-1)
 
 
 def bf16_half_ulp(v: torch.Tensor) -> torch.Tensor:

@@ -539,6 +539,10 @@ DecodeShape decode_shape(int64_t B, int Hq, int Hkv, int64_t Sq, int64_t Skv,
 
 using namespace q35;
 
+int q35_attn_prefill_tc(const void *q, const void *k, const void *v, void *out,
+                        float *lse, int64_t B, int Hq, int Hkv, int64_t Sq,
+                        int64_t Skv, float scale, int causal, q35_stream_t stream);
+
 extern "C" int q35_attn_prefill_fwd(const void *q, const void *k, const void *v,
                                     void *out, float *lse, int64_t B, int Hq,
                                     int Hkv, int64_t Sq, int64_t Skv, int D,
@@ -553,6 +557,8 @@ extern "C" int q35_attn_prefill_fwd(const void *q, const void *k, const void *v,
     return fail(Q35_ERR_ALIGN, "attn_prefill: pointers not 16-byte aligned");
   if (B * Sq == 0) return Q35_OK;
   if (B * Hq > 65535) return fail(Q35_ERR_SHAPE, "attn_prefill: B*Hq > 65535");
+  if (D == 128)  // tcgen05 path
+    return q35_attn_prefill_tc(q, k, v, out, lse, B, Hq, Hkv, Sq, Skv, scale, causal, stream);
   dim3 grid(static_cast<unsigned>((Sq + kPM - 1) / kPM), static_cast<unsigned>(B * Hq));
   auto run = [&](auto kern, int smem) -> int {
     Q35_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
