@@ -176,11 +176,12 @@ def staged_forward(layer, rot, x, pos, marks=None):
     mark("router")
     perm = K.moe_permute(idx, moe.num_experts)
     mark("permute")
+    gu_p, dn_p = moe._packed_experts()
     xs = K.gather_rows(m2, perm.sorted_tok)
     mark("gather")
-    act = K.grouped_gateup_swiglu(xs, moe.gate_up_proj, perm)
+    act = K.grouped_gateup_swiglu(xs, moe.gate_up_proj, perm, w_packed=gu_p)
     mark("gate_up_swiglu")
-    y = K.grouped_down(act, moe.down_proj, perm)
+    y = K.grouped_down(act, moe.down_proj, perm, w_packed=dn_p)
     mark("down")
     out = K.moe_combine(y, wts, perm.slot_pos, h.reshape(-1, H), B * S, H)
     mark("combine_residual")

@@ -218,16 +218,25 @@ Q35_API int q35_gemm_bf16_f32out(const void *a, const void *b, const void *bias,
  *          modules/moe.py:77-80, csrc/swiglu_op.cu:6-18).
  * down:    y[r, n] = bf16( act[r,:].w[e, n, :] ); w = down_proj [E, H, I].
  *          Replaces matmul(activated, down_proj[e]) (REF modules/moe.py:81).
- * offsets/tile_offsets are device arrays ([E+1]); rows_cap bounds R.        */
+ * offsets/tile_offsets are device arrays ([E+1]); rows_cap bounds R.
+ * w_packed != 0: the weight is the q35_pack_b_tiles copy of the same tensor.  */
 Q35_API int q35_grouped_gemm_gateup_swiglu(const void *a, const void *w_gate_up,
-                                   void *act, const int32_t *offsets,
-                                   const int32_t *tile_offsets, int E,
-                                   int64_t rows_cap, int H, int I,
-                                   q35_stream_t stream);
+                                           void *act, const int32_t *offsets,
+                                           const int32_t *tile_offsets, int E,
+                                           int64_t rows_cap, int H, int I,
+                                           int w_packed, q35_stream_t stream);
 Q35_API int q35_grouped_gemm_down(const void *act, const void *w_down, void *y,
-                          const int32_t *offsets, const int32_t *tile_offsets,
-                          int E, int64_t rows_cap, int H, int I,
-                          q35_stream_t stream);
+                                  const int32_t *offsets, const int32_t *tile_offsets,
+                                  int E, int64_t rows_cap, int H, int I,
+                                  int w_packed, q35_stream_t stream);
+
+/* Packs a K-major bf16 weight matrix [rows, K] (rows % 128 == 0, K % 64 == 0)
+ * into contiguous 128-row x 64-column tiles (tile (r, k) at element offset
+ * ((r * K/64) + k) * 8192).  The grouped GEMMs read such a copy when called
+ * with w_packed != 0: every weight tile is then one contiguous 16 KB read.
+ * No reference counterpart (a storage format of this library).               */
+Q35_API int q35_pack_b_tiles(const void *src, void *dst, int64_t rows, int64_t K,
+                             q35_stream_t stream);
 
 /* ---- Combine --------------------------------------------------------------
  * out[t,:] = bf16( residual[t,:] + sum_j weights[t,j] * y[slot_pos[t*k+j],:] )

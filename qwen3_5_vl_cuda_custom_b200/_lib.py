@@ -46,9 +46,10 @@ _SIGS = {
     "q35_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                               c_int64, c_void_p]),
     "q35_grouped_gemm_gateup_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-                                               c_int, c_int64, c_int, c_int, c_void_p]),
+                                               c_int, c_int64, c_int, c_int, c_int, c_void_p]),
     "q35_grouped_gemm_down": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
-                                      c_int64, c_int, c_int, c_void_p]),
+                                      c_int64, c_int, c_int, c_int, c_void_p]),
+    "q35_pack_b_tiles": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
     "q35_moe_combine": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int64,
                                 c_int, c_int64, c_void_p]),
     "q35_rmsnorm_f32in_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float,

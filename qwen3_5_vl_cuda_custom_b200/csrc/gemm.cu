@@ -61,6 +61,7 @@ struct GemmParams {
   int a_k_wrap;                // > 0: A's K coordinate wraps at this width
   int k_splits;                // dense only: K split into this many partial planes
   int64_t split_stride;        // elements between partial output planes
+  int b_packed;                // B stored as contiguous 128 x 64 tiles (see q35_pack_b_tiles)
 };
 
 template <int BN, int STAGES>
@@ -371,6 +372,309 @@ int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb,
   return Q35_OK;
 }
 
+
+// ---------------------------------------------------------------------------
+// 2-SM variant: a CTA pair (cluster of 2) computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256 across the two SMs' tensor memories).
+// Each CTA loads its own 128 rows of A and 128 rows of B per k-block (32 KB,
+// half of what one CTA needs for a 128 x 256 tile), so the L2->SM traffic per
+// FLOP halves and 6 stages fit.  Both CTAs' TMA loads complete on the leader's
+// full barrier (the leader alone expects the 64 KB); the leader issues the MMAs
+// and its commits arrive on both CTAs' barriers; each CTA's epilogue drains its
+// own 128 accumulator rows and arrives on the leader's accumulator-empty
+// barrier.  No TMA multicast is used.
+struct PairLayout {
+  static constexpr int kStages = 6;
+  static constexpr int kHalf = 128 * kBK * 2;           // 16 KB
+  static constexpr int kStageBytes = 2 * kHalf;         // A half + B half
+  static constexpr int kBarOff = kStages * kStageBytes;
+  static constexpr int kNumBars = 2 * kStages + 5;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kGroupOff = kMiscOff + 16;
+  static constexpr int bytes(int E) { return 1024 + kGroupOff + 2 * (E + 1) * 4; }
+};
+
+__device__ __forceinline__ TileInfo decode_pair_tile(int tile, const GemmParams &p,
+                                                     const int *s_off, const int *s_pt) {
+  TileInfo ti;
+  ti.split = 0;
+  if (p.offsets == nullptr) {
+    // Rasterise in bands of 8 M tiles: CTAs running together share 8 A tiles
+    // and a run of B tiles in L2, whatever the aspect ratio of the problem.
+    const int mtiles = (p.M + 255) / 256;
+    const int band = tile / (8 * p.n_tiles);
+    const int band_m = min(8, mtiles - band * 8);
+    const int in_band = tile - band * 8 * p.n_tiles;
+    ti.nt = in_band / band_m;
+    const int mt = band * 8 + (in_band - ti.nt * band_m);
+    ti.group = 0;
+    ti.row0 = mt * 256;
+    ti.rows_valid = min(256, p.M - ti.row0);
+    return ti;
+  }
+  int lo = 0, hi = p.E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (s_pt[mid] * p.n_tiles <= tile) lo = mid; else hi = mid - 1;
+  }
+  while (lo < p.E - 1 && s_pt[lo + 1] * p.n_tiles <= tile) ++lo;
+  const int e = lo;
+  const int me = s_pt[e + 1] - s_pt[e];
+  const int local = tile - s_pt[e] * p.n_tiles;
+  ti.nt = local / me;
+  const int mt = local - ti.nt * me;
+  ti.group = e;
+  ti.row0 = s_off[e] + mt * 256;
+  ti.rows_valid = min(256, s_off[e + 1] - ti.row0);
+  return ti;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  using L = PairLayout;
+  constexpr int BN = 256;
+  constexpr int S = L::kStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L::kBarOff);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + S;
+  uint64_t *tfull = bars + 2 * S;
+  uint64_t *tempty = bars + 2 * S + 2;
+  uint64_t *drain = bars + 2 * S + 4;
+  uint32_t *s_tmem = reinterpret_cast<uint32_t *>(smem + L::kMiscOff);
+  int *s_off = reinterpret_cast<int *>(smem + L::kGroupOff);
+  int *s_pt = s_off + (p.E + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = sm100::cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (p.offsets != nullptr) {
+    for (int i = threadIdx.x; i <= p.E; i += kThreads) s_off[i] = p.offsets[i];
+  }
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      sm100::mbar_init(&full[i], 1);
+      sm100::mbar_init(&empty[i], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      sm100::mbar_init(&tfull[a], 1);
+      sm100::mbar_init(&tempty[a], 256);
+    }
+    sm100::mbar_init(drain, 1);
+    sm100::fence_mbar_init();
+    sm100::prefetch_tensormap(&tmA);
+    sm100::prefetch_tensormap(&tmB);
+  }
+  __syncthreads();
+  if (p.offsets != nullptr && threadIdx.x == 0) {
+    // 256-row M tiles per group (prefix over groups).
+    int acc = 0;
+    s_pt[0] = 0;
+    for (int e = 0; e < p.E; ++e) {
+      acc += (s_off[e + 1] - s_off[e] + 255) / 256;
+      s_pt[e + 1] = acc;
+    }
+  }
+  if (warp == 1) sm100::tmem_alloc_pair(s_tmem, 2 * BN);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::cluster_sync();  // barriers of both CTAs initialised before any remote use
+  sm100::tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+
+  const int total = (p.offsets == nullptr) ? ((p.M + 255) / 256) * p.n_tiles
+                                           : s_pt[p.E] * p.n_tiles;
+  const int k_blocks = (p.K + kBK - 1) / kBK;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------ TMA producer (both CTAs)
+    uint32_t g = 0;
+    bool ok = true;
+    for (int tile = pair; tile < total && ok; tile += npairs) {
+      const TileInfo ti = decode_pair_tile(tile, p, s_off, s_pt);
+      const int arow = ti.row0 + static_cast<int>(rank) * 128;
+      const int brow = ti.group * p.b_rows_per_group + ti.nt * p.b_tile_step +
+                       static_cast<int>(rank) * p.b_second_off;
+      for (int kb = 0; kb < k_blocks; ++kb, ++g) {
+        const int st = g % S;
+        const uint32_t ph = (g / S) & 1u;
+        if (!sm100::mbar_wait(&empty[st], ph ^ 1u)) {
+          report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 211, tile, kb);
+          ok = false;
+          break;
+        }
+        uint8_t *sa = smem + st * L::kStageBytes;
+        uint8_t *sb = sa + L::kHalf;
+        const uint32_t leader_full = sm100::mapa_shared(sm100::smem_u32(&full[st]), 0);
+        if (rank == 0) sm100::mbar_arrive_expect_tx(&full[st], 2 * L::kStageBytes);
+        sm100::tma_load_2d_pair(sa, &tmA, leader_full, kb * kBK, arow);
+        if (p.b_packed)  // tile (brow / 128, kb) is 16 KB contiguous
+          sm100::tma_load_2d_pair(sb, &tmB, leader_full, 0, ((brow >> 7) * k_blocks + kb) * 128);
+        else
+          sm100::tma_load_2d_pair(sb, &tmB, leader_full, kb * kBK, brow);
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ------------------------------------------------ MMA issuer (leader CTA)
+    constexpr uint32_t idesc = sm100::idesc_bf16_f32(256, BN);
+    uint32_t g = 0, j = 0;
+    bool ok = true;
+    for (int tile = pair; tile < total && ok; tile += npairs, ++j) {
+      const uint32_t acc = j & 1u, use = j >> 1;
+      if (!sm100::mbar_wait(&tempty[acc], (use & 1u) ^ 1u)) {
+        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 212, tile, 0);
+        break;
+      }
+      sm100::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < k_blocks; ++kb, ++g) {
+        const int st = g % S;
+        const uint32_t ph = (g / S) & 1u;
+        if (!sm100::mbar_wait(&full[st], ph)) {
+          report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 213, tile, kb);
+          ok = false;
+          break;
+        }
+        sm100::tc_fence_after();
+        const uint32_t sa = sm100::smem_u32(smem + st * L::kStageBytes);
+        const uint64_t adesc = sm100::sw128_kmajor_desc(sa);
+        const uint64_t bdesc = sm100::sw128_kmajor_desc(sa + L::kHalf);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)
+          sm100::mma_bf16_ss_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc,
+                                  (kb | kk) != 0 ? 1u : 0u);
+        sm100::mma_commit_pair_mc(&empty[st], 0x3);
+      }
+      sm100::mma_commit_pair_mc(&tfull[acc], 0x3);
+    }
+    sm100::mma_commit_pair_mc(drain, 0x1);
+    if (!sm100::mbar_wait(drain, 0)) report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 214, 0, 0);
+  } else if (warp >= 2) {
+    // ------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int r_in_tile = static_cast<int>(rank) * 128 + q * 32 + lane;
+    uint32_t j = 0;
+    for (int tile = pair; tile < total; tile += npairs, ++j) {
+      const TileInfo ti = decode_pair_tile(tile, p, s_off, s_pt);
+      const uint32_t acc = j & 1u, use = j >> 1;
+      if (!sm100::mbar_wait(&tfull[acc], use & 1u)) {
+        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 215, tile, static_cast<int>(rank));
+        break;
+      }
+      sm100::tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      const bool valid = r_in_tile < ti.rows_valid;
+      const int64_t row = static_cast<int64_t>(ti.row0) + r_in_tile;
+      if constexpr (EPI == EPI_PLAIN) {
+        const int n0 = ti.nt * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld32(t_row + c * 32, r);
+          sm100::tmem_wait_ld();
+          const int col = n0 + c * 32;
+          if (valid && col < p.N) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+            if (p.bias) {
+              float bv[32];
+              load32(p.bias + col, bv);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] += bv[i];
+            }
+            if (p.residual) {
+              float rv[32];
+              load32(p.residual + row * p.ldr + col, rv);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = rv[i] + v[i];
+            }
+            if (p.out_f32) {
+              float4 *o = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.out) + row * p.ldo + col);
+#pragma unroll
+              for (int qq = 0; qq < 8; ++qq)
+                o[qq] = make_float4(v[4 * qq], v[4 * qq + 1], v[4 * qq + 2], v[4 * qq + 3]);
+            } else {
+              store32(p.out + row * p.ldo + col, v);
+            }
+          }
+        }
+      } else {
+        const int n0 = ti.nt * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t rg[32], ru[32];
+          sm100::tmem_ld32(t_row + c * 32, rg);
+          sm100::tmem_ld32(t_row + BN / 2 + c * 32, ru);
+          sm100::tmem_wait_ld();
+          const int col = n0 + c * 32;
+          if (valid && col < p.N) {
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              v[i] = silu(__uint_as_float(rg[i])) * __uint_as_float(ru[i]);
+            store32(p.out + row * p.ldo + col, v);
+          }
+        }
+      }
+      sm100::tc_fence_before();
+      sm100::mbar_arrive_cluster(sm100::mapa_shared(sm100::smem_u32(&tempty[acc]), 0));
+    }
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::cluster_sync();  // no CTA leaves while its peer may still signal it
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc_pair(tmem_base, 2 * BN);
+  }
+}
+
+template <int EPI>
+int launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
+                     int max_pair_tiles, cudaStream_t s) {
+  const int smem = PairLayout::bytes(p.E);
+  auto kern = gemm_pair_kernel<EPI>;
+  Q35_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int npairs = max(1, min(max_pair_tiles, num_sms() / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * npairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  Q35_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+  return Q35_OK;
+}
+
+
+// dst tile (rb, kb) = src rows [128 rb, 128 rb + 128) x cols [64 kb, 64 kb + 64),
+// stored row-major as 128 x 64 contiguous elements (16 KB); one thread moves 16 B.
+__global__ void pack_b_tiles_kernel(const uint16_t *__restrict__ src,
+                                    uint16_t *__restrict__ dst, int64_t rows, int64_t K) {
+  const int64_t kb_n = K / 64;
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // 16-B chunk
+  if (i >= rows * (K / 8)) return;
+  const int64_t r = i / (K / 8), c8 = i % (K / 8);
+  const int64_t kb = c8 / 8, cin = (c8 % 8) * 8;
+  const int64_t rb = r / 128, rin = r % 128;
+  const int64_t d = ((rb * kb_n + kb) * 128 + rin) * 64 + cin;
+  *reinterpret_cast<uint4 *>(dst + d) = *reinterpret_cast<const uint4 *>(src + r * K + c8 * 8);
+}
+
 }  // namespace
 }  // namespace q35
 
@@ -397,7 +701,10 @@ static int gemm_dense(const void *a, const void *b, const void *bias,
   // Pick the N tile that finishes the last wave soonest (time ~ waves * BN).
   const int64_t t256 = mt * ((N + 255) / 256), t128 = mt * ((N + 127) / 128);
   const int64_t cost256 = ((t256 + sms - 1) / sms) * 2, cost128 = (t128 + sms - 1) / sms;
-  const int BN = (cost256 <= cost128 && N % 256 == 0) ? 256 : 128;
+  // 256-wide tiles run on CTA pairs (cta_group::2), which sustain a higher
+  // fraction of peak than single-CTA 128-wide tiles: prefer them unless they
+  // would need clearly more waves.
+  const int BN = (N % 256 == 0 && cost256 <= cost128 + 2) ? 256 : 128;
   CUtensorMap ta, tb;
   int st = make_tmap_bf16_2d(&ta, a, K, M, K * 2, kBK, kBM);
   if (st) return st;
@@ -421,7 +728,14 @@ static int gemm_dense(const void *a, const void *b, const void *bias,
   p.out_f32 = out_f32;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   const int tiles = static_cast<int>(mt * p.n_tiles);
-  if (BN == 256) return launch_gemm<256, EPI_PLAIN, 4>(ta, tb, p, tiles, s);
+  if (BN == 256) {
+    // CTA pairs (cta_group::2) on 256 x 256 tiles; B boxes are 128 rows per CTA.
+    CUtensorMap tb2;
+    st = make_tmap_bf16_2d(&tb2, b, K, N, K * 2, kBK, 128);
+    if (st) return st;
+    const int pair_tiles = static_cast<int>(((M + 255) / 256) * p.n_tiles);
+    return launch_gemm_pair<EPI_PLAIN>(ta, tb2, p, pair_tiles, s);
+  }
   return launch_gemm<128, EPI_PLAIN, 6>(ta, tb, p, tiles, s);
 }
 
@@ -487,10 +801,29 @@ extern "C" int q35_router_logits_tc(const void *x, const void *w3,
   return launch_gemm<BN, EPI_PLAIN, 8>(ta, tb, p, tiles, reinterpret_cast<cudaStream_t>(stream));
 }
 
+// Re-lays a K-major bf16 matrix [rows, K] (e.g. all experts' weights,
+// rows = E * R) as contiguous 128-row x 64-column tiles, so that every TMA box
+// the grouped GEMM loads is one 16 KB contiguous read instead of 128 strided
+// 128-byte segments.  rows % 128 == 0, K % 64 == 0.
+extern "C" int q35_pack_b_tiles(const void *src, void *dst, int64_t rows, int64_t K,
+                                q35_stream_t stream) {
+  if (!src || !dst) return fail(Q35_ERR_INVALID, "pack_b_tiles: null pointer");
+  if (rows <= 0 || K <= 0 || rows % 128 != 0 || K % 64 != 0)
+    return fail(Q35_ERR_SHAPE, "pack_b_tiles: rows %lld (x128) K %lld (x64)", (long long)rows,
+                (long long)K);
+  if (!aligned16(src) || !aligned16(dst)) return fail(Q35_ERR_ALIGN, "pack_b_tiles: alignment");
+  const int64_t n = rows * (K / 8);
+  pack_b_tiles_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
+                        reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t *>(src), static_cast<uint16_t *>(dst), rows, K);
+  Q35_LAUNCH_CHECK("pack_b_tiles launch");
+  return Q35_OK;
+}
+
 static int grouped_common(const void *a, const void *w, void *out,
                           const int32_t *offsets, const int32_t *tile_offsets,
                           int E, int64_t rows_cap, int64_t K, int64_t N_out,
-                          int64_t b_rows_per_group, int swiglu,
+                          int64_t b_rows_per_group, int swiglu, int packed,
                           q35_stream_t stream) {
   if (!a || !w || !out || !offsets || !tile_offsets)
     return fail(Q35_ERR_INVALID, "grouped_gemm: null pointer");
@@ -509,8 +842,16 @@ static int grouped_common(const void *a, const void *w, void *out,
   CUtensorMap ta, tb;
   int st = make_tmap_bf16_2d(&ta, a, K, rows_cap, K * 2, kBK, kBM);
   if (st) return st;
-  st = make_tmap_bf16_2d(&tb, w, K, static_cast<uint64_t>(E) * b_rows_per_group,
-                         K * 2, kBK, BN / 2);
+  if (packed) {
+    if (K % kBK != 0 || b_rows_per_group % 128 != 0 || (swiglu && N_out % 128 != 0))
+      return fail(Q35_ERR_SHAPE, "grouped_gemm: packed weights need K %% 64, rows %% 128");
+    // packed tiles viewed as [E * R * K / 64, 64] rows of 128 B
+    st = make_tmap_bf16_2d(&tb, w, kBK, static_cast<uint64_t>(E) * b_rows_per_group * (K / kBK),
+                           kBK * 2, kBK, BN / 2);
+  } else {
+    st = make_tmap_bf16_2d(&tb, w, K, static_cast<uint64_t>(E) * b_rows_per_group,
+                           K * 2, kBK, BN / 2);
+  }
   if (st) return st;
   GemmParams p{};
   p.offsets = offsets;
@@ -526,29 +867,34 @@ static int grouped_common(const void *a, const void *w, void *out,
   p.out = static_cast<uint16_t *>(out);
   p.ldo = N_out;
   p.err = err;
+  p.b_packed = packed ? 1 : 0;
   // Upper bound on tiles: every group may add one partial M tile.
   const int64_t max_tiles = ((rows_cap + kBM - 1) / kBM + E) * p.n_tiles;
   const int mt = static_cast<int>(max_tiles < (1 << 30) ? max_tiles : (1 << 30));
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (swiglu) return launch_gemm<BN, EPI_SWIGLU, 4>(ta, tb, p, mt, s);
-  return launch_gemm<BN, EPI_PLAIN, 4>(ta, tb, p, mt, s);
+  // CTA pairs (cta_group::2): 256-row tiles per group, B boxes of 128 rows.
+  const int64_t max_pair = ((rows_cap + 255) / 256 + E) * p.n_tiles;
+  const int mp = static_cast<int>(max_pair < (1 << 30) ? max_pair : (1 << 30));
+  (void)mt;
+  if (swiglu) return launch_gemm_pair<EPI_SWIGLU>(ta, tb, p, mp, s);
+  return launch_gemm_pair<EPI_PLAIN>(ta, tb, p, mp, s);
 }
 
 extern "C" int q35_grouped_gemm_gateup_swiglu(
     const void *a, const void *w_gate_up, void *act, const int32_t *offsets,
     const int32_t *tile_offsets, int E, int64_t rows_cap, int H, int I,
-    q35_stream_t stream) {
+    int w_packed, q35_stream_t stream) {
   if (H <= 0 || I <= 0) return fail(Q35_ERR_SHAPE, "gate_up: bad H/I");
   return grouped_common(a, w_gate_up, act, offsets, tile_offsets, E, rows_cap,
-                        H, I, 2 * static_cast<int64_t>(I), 1, stream);
+                        H, I, 2 * static_cast<int64_t>(I), 1, w_packed, stream);
 }
 
 extern "C" int q35_grouped_gemm_down(const void *act, const void *w_down,
                                      void *y, const int32_t *offsets,
                                      const int32_t *tile_offsets, int E,
                                      int64_t rows_cap, int H, int I,
-                                     q35_stream_t stream) {
+                                     int w_packed, q35_stream_t stream) {
   if (H <= 0 || I <= 0) return fail(Q35_ERR_SHAPE, "down: bad H/I");
   return grouped_common(act, w_down, y, offsets, tile_offsets, E, rows_cap, I,
-                        H, H, 0, stream);
+                        H, H, 0, w_packed, stream);
 }

@@ -233,31 +233,47 @@ def gather_rows(src: torch.Tensor, rows: torch.Tensor, n_dev: torch.Tensor | Non
     return dst
 
 
+def pack_b_tiles(w: torch.Tensor) -> torch.Tensor:
+    """Copy of a bf16 weight [..., rows, K] as contiguous 128 x 64 tiles (the
+    layout the grouped GEMMs stream with one 16 KB read per TMA box)."""
+    w = _require(w, "pack_b_tiles.w")
+    K = w.shape[-1]
+    rows = w.numel() // K
+    out = torch.empty_like(w)
+    with torch.cuda.device(w.device):
+        _lib.call("q35_pack_b_tiles", w.data_ptr(), out.data_ptr(), rows, K, _stream(w))
+    return out
+
+
 def grouped_gateup_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, perm: Permutation,
-                          rows_cap: int | None = None) -> torch.Tensor:
-    """act[r] = silu(a[r] @ Wg[e]^T) * (a[r] @ Wu[e]^T) for the rows of each expert e."""
+                          rows_cap: int | None = None,
+                          w_packed: torch.Tensor | None = None) -> torch.Tensor:
+    """act[r] = silu(a[r] @ Wg[e]^T) * (a[r] @ Wu[e]^T) for the rows of each expert e.
+    ``w_packed`` (pack_b_tiles(w_gate_up)) is read instead of w_gate_up if given."""
     a = _require(a, "gate_up.a")
-    w = _require(w_gate_up, "gate_up.w")
-    E, I2, H = w.shape
+    w = _require(w_gate_up if w_packed is None else w_packed, "gate_up.w")
+    E, I2, H = w_gate_up.shape
     R = a.shape[0] if rows_cap is None else rows_cap
     act = torch.empty(R, I2 // 2, device=a.device, dtype=a.dtype)
     with torch.cuda.device(a.device):
         _lib.call("q35_grouped_gemm_gateup_swiglu", a.data_ptr(), w.data_ptr(), act.data_ptr(),
                   perm.offsets.data_ptr(), perm.tile_offsets.data_ptr(), E, R, H, I2 // 2,
-                  _stream(a))
+                  0 if w_packed is None else 1, _stream(a))
     return act
 
 
-def grouped_down(act: torch.Tensor, w_down: torch.Tensor, perm: Permutation) -> torch.Tensor:
-    """y[r] = act[r] @ Wd[e]^T for the rows of each expert e."""
+def grouped_down(act: torch.Tensor, w_down: torch.Tensor, perm: Permutation,
+                 w_packed: torch.Tensor | None = None) -> torch.Tensor:
+    """y[r] = act[r] @ Wd[e]^T for the rows of each expert e (``w_packed`` as above)."""
     act = _require(act, "down.act")
-    w = _require(w_down, "down.w")
-    E, H, I = w.shape
+    w = _require(w_down if w_packed is None else w_packed, "down.w")
+    E, H, I = w_down.shape
     R = act.shape[0]
     y = torch.empty(R, H, device=act.device, dtype=act.dtype)
     with torch.cuda.device(act.device):
         _lib.call("q35_grouped_gemm_down", act.data_ptr(), w.data_ptr(), y.data_ptr(),
-                  perm.offsets.data_ptr(), perm.tile_offsets.data_ptr(), E, R, H, I, _stream(act))
+                  perm.offsets.data_ptr(), perm.tile_offsets.data_ptr(), E, R, H, I,
+                  0 if w_packed is None else 1, _stream(act))
     return y
 
 
@@ -362,7 +378,7 @@ def device_error_check():
 
 __all__ = [
     "rmsnorm", "matmul", "softmax", "cuda_topk", "cuda_index_add", "swiglu", "residual_add",
-    "router_topk", "moe_permute", "Permutation", "gather_rows", "grouped_gateup_swiglu",
+    "router_topk", "router_split_weights", "pack_b_tiles", "moe_permute", "Permutation", "gather_rows", "grouped_gateup_swiglu",
     "grouped_down", "moe_combine", "qknorm_mrope", "mrope", "attention_tokens",
     "flash_attention", "device_error_check", "default_scale",
 ]

@@ -324,6 +324,26 @@ class CudaSparseMoE(nn.Module):
             self._split_cache = cache
         return cache[1]
 
+    pack_expert_weights = False
+
+    def _packed_experts(self):
+        """Tile-packed copies of gate_up_proj / down_proj (contiguous 16 KB TMA
+        boxes), rebuilt when a weight is replaced or modified in place.  Off by
+        default: it costs one extra copy of the expert weights and measured no
+        faster than streaming the parameters (``pack_expert_weights = True``
+        enables it)."""
+        I, H = self.moe_intermediate_size, self.hidden_size
+        if not self.pack_expert_weights or I % 128 or H % 128:
+            return None, None
+        key = _params_key(self.gate_up_proj, self.down_proj)
+        cache = getattr(self, "_pack_cache", None)
+        if cache is None or cache[0] != key:
+            with torch.no_grad():
+                cache = (key, K.pack_b_tiles(self.gate_up_proj.detach()),
+                         K.pack_b_tiles(self.down_proj.detach()))
+            self._pack_cache = cache
+        return cache[1], cache[2]
+
     def route(self, x2d: torch.Tensor):
         """Router only: (logits fp32 (T,E), top-k ids int32 (T,k), weights fp32 (T,k))."""
         return K.router_topk(x2d, self.gate_weight, self.top_k, self.norm_topk_prob,
@@ -333,10 +353,11 @@ class CudaSparseMoE(nn.Module):
                 residual: torch.Tensor | None = None) -> torch.Tensor:
         """Expert compute + weighted combine for routed tokens (T,H) -> (T,H)."""
         T, H = x2d.shape
+        gu_p, dn_p = self._packed_experts()
         perm = K.moe_permute(idx, self.num_experts)
         xs = K.gather_rows(x2d, perm.sorted_tok)
-        act = K.grouped_gateup_swiglu(xs, self.gate_up_proj, perm)
-        y = K.grouped_down(act, self.down_proj, perm)
+        act = K.grouped_gateup_swiglu(xs, self.gate_up_proj, perm, w_packed=gu_p)
+        y = K.grouped_down(act, self.down_proj, perm, w_packed=dn_p)
         return K.moe_combine(y, weights, perm.slot_pos, residual, T, H)
 
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None):

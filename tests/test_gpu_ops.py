@@ -204,6 +204,10 @@ def test_moe_experts_pipeline(T, H, I, E, k):
     assert torch.equal(xs.cpu(), x[perm.sorted_tok.cpu().long()])
     act = Kk.grouped_gateup_swiglu(xs, gu.to(DEV), perm)
     y = Kk.grouped_down(act, dn.to(DEV), perm)
+    if I % 128 == 0 and H % 128 == 0:  # tile-packed weights give identical results
+        act_p = Kk.grouped_gateup_swiglu(xs, gu.to(DEV), perm, w_packed=Kk.pack_b_tiles(gu.to(DEV)))
+        y_p = Kk.grouped_down(act, dn.to(DEV), perm, w_packed=Kk.pack_b_tiles(dn.to(DEV)))
+        assert torch.equal(act_p, act) and torch.equal(y_p, y)
     out = Kk.moe_combine(y, w, perm.slot_pos, res.to(DEV), T, H).float().cpu()
     # oracle with the GPU's own routing (routing parity is tested separately)
     offs = perm.offsets.cpu().tolist()
