@@ -8,6 +8,10 @@ inputs (synthetic: no checkpoint or dataset).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
+``value`` times the forward replayed from a CUDA graph of the module call
+(qwen3_5_vl_cuda_custom_b200.graphs.GraphedDecoderLayer); the eager module
+call is reported beside it.
+
 One process per GPU (torchrun for N > 1).  Each rank runs the full layer on
 its own 4096-token sequence (data-parallel over sequences, experts
 replicated: "replicas"), so per-GPU work is fixed ("scaling": "weak").
@@ -318,50 +322,56 @@ def run_ours(args, world, rank, local):
         for _ in range(max(3, args.warmup)):
             layer(x, bpos)
         barrier(world)
-        # ---------------- device-timed steps
-        times = []
-        if True:
+        # ---------------- device-timed steps: eager module calls, then the
+        # same forward replayed from a CUDA graph (GraphedDecoderLayer)
+        from qwen3_5_vl_cuda_custom_b200.graphs import GraphedDecoderLayer
+
+        def timed(step_fn):
+            times = []
             barrier(world)
             for _ in range(args.steps):
                 flush.zero_()
                 s0 = torch.cuda.Event(enable_timing=True)
                 s1 = torch.cuda.Event(enable_timing=True)
                 s0.record()
-                layer(x, bpos)
+                step_fn()
                 s1.record()
                 times.append((s0, s1))
             barrier(world)
-        step_ms = [a.elapsed_time(b) for a, b in times]
-        total_ms = allreduce_max(sum(step_ms), world)
-        ms_per_step = total_ms / args.steps
-        value = world * T * args.steps / (total_ms / 1e3)
+            return allreduce_max(sum(a.elapsed_time(b) for a, b in times), world)
+
+        eager_ms = timed(lambda: layer(x, bpos))
 
         # ---------------- per-stage breakdown (same kernels, events between)
-        stage_ms: dict[str, float] = {}
-        reps = 5
-        for _ in range(reps):
+        samples: dict[str, list[float]] = {}
+        for _ in range(7):
             flush.zero_()
             marks = []
             staged_forward(layer, rot, x, pos, marks)
             torch.cuda.synchronize()
             for (_, a), (name, b) in zip(marks[:-1], marks[1:]):
-                stage_ms[name] = stage_ms.get(name, 0.0) + a.elapsed_time(b) / reps
+                samples.setdefault(name, []).append(a.elapsed_time(b))
+        stage_ms = {k: statistics.median(v) for k, v in samples.items()}
 
-        # ---------------- end to end through the public module API
+        graphed = GraphedDecoderLayer(layer, rot, x, pos)
+        total_ms = timed(graphed.replay)
+        ms_per_step = total_ms / args.steps
+        value = world * T * args.steps / (total_ms / 1e3)
+        eager_value = world * T * args.steps / (eager_ms / 1e3)
+
+        # ---------------- end to end through the public API: StreamedLayerRunner
+        # copies each step's input from pinned host memory and its output back,
+        # overlapping the copies with the neighbouring steps' replays
+        from qwen3_5_vl_cuda_custom_b200.graphs import StreamedLayerRunner
         x_host = x_cpu.to(torch.bfloat16).pin_memory()
         out_host = torch.empty_like(x_host).pin_memory()
-        for _ in range(2):
-            xd = x_host.to(dev, non_blocking=True)
-            y, _, _ = layer(xd, bpos)
-            out_host.copy_(y, non_blocking=True)
+        runner = StreamedLayerRunner(graphed)
+        runner.run(x_host, out_host, 2)
         barrier(world)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.steps):
-            xd = x_host.to(dev, non_blocking=True)
-            y, _, _ = layer(xd, bpos)
-            out_host.copy_(y, non_blocking=True)
+        runner.run(x_host, out_host, args.steps)
         e1.record()
         barrier(world)
         e2e_ms = allreduce_max(e0.elapsed_time(e1), world)
@@ -421,7 +431,10 @@ def run_ours(args, world, rank, local):
                    "parallelism": f"dp{world} sequences, experts replicated",
                    "l2": "256 MiB flush between timed steps"},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": in_bytes,
-                "d2h_bytes_per_step": in_bytes},
+                "d2h_bytes_per_step": in_bytes,
+                "api": "StreamedLayerRunner(GraphedDecoderLayer)"},
+        "eager": {"value": eager_value, "ms_per_step": eager_ms / args.steps,
+                  "note": "same layer through the module API without graph replay"},
         "gpu_launches": LAUNCHES_PER_LAYER * args.steps,
         "roofline": {"bound": bound, "kernel": top, "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak, "traffic": None, "peak_source": peak_src},

@@ -561,7 +561,7 @@ extern "C" int q35_attn_prefill_fwd(const void *q, const void *k, const void *v,
     return q35_attn_prefill_tc(q, k, v, out, lse, B, Hq, Hkv, Sq, Skv, scale, causal, stream);
   dim3 grid(static_cast<unsigned>((Sq + kPM - 1) / kPM), static_cast<unsigned>(B * Hq));
   auto run = [&](auto kern, int smem) -> int {
-    Q35_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    { const int _st = ensure_smem_attr(reinterpret_cast<const void *>(kern), smem); if (_st) return _st; }
     kern<<<grid, kPThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
         static_cast<const uint16_t *>(v), static_cast<uint16_t *>(out), lse, Hq,
@@ -608,7 +608,7 @@ extern "C" int q35_attn_decode_fwd(const void *q, const void *k, const void *v,
   const int64_t rows = B * Hkv * sh.R;
   const unsigned mgrid = static_cast<unsigned>((rows + 7) / 8);
   auto run = [&](auto kern, auto merge, int smem) -> int {
-    Q35_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    { const int _st = ensure_smem_attr(reinterpret_cast<const void *>(kern), smem); if (_st) return _st; }
     kern<<<grid, kDThreads, smem, s>>>(
         static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
         static_cast<const uint16_t *>(v), workspace, sh);

@@ -340,8 +340,7 @@ int q35_attn_prefill_tc(const void *q, const void *k, const void *v, void *out,
   p.out = static_cast<uint16_t *>(out);
   p.lse = lse;
   p.err = err;
-  Q35_CHECK_CUDA(cudaFuncSetAttribute(attn_tc_kernel,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+  { const int _st = ensure_smem_attr(reinterpret_cast<const void *>(attn_tc_kernel), kSmem); if (_st) return _st; }
   dim3 grid(p.n_mblocks, static_cast<unsigned>(B * Hq));
   attn_tc_kernel<<<grid, kThreads, kSmem, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
   Q35_LAUNCH_CHECK("attn_prefill_tc launch");

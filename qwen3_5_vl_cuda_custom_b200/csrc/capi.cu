@@ -4,7 +4,9 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "sm100.cuh"
 
@@ -61,6 +63,22 @@ int num_sms() {
     g_num_sms[dev] = n > 0 ? n : 1;
   }
   return g_num_sms[dev];
+}
+
+int ensure_smem_attr(const void *kernel, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void *>, int> done;
+  int dev = 0;
+  int st = current_device(&dev);
+  if (st) return st;
+  std::lock_guard<std::mutex> lk(mu);
+  auto key = std::make_pair(dev, kernel);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return Q35_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+  done[key] = bytes;
+  return Q35_OK;
 }
 
 int make_tmap_bf16_2d(CUtensorMap *map, const void *base, uint64_t inner,

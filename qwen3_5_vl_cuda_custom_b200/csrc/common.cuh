@@ -21,6 +21,10 @@ int cuda_fail(cudaError_t e, const char *what);
 int *device_error_word();
 // Number of SMs of the current device (cached).
 int num_sms();
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the current
+// device, once (cached per device and kernel) so launches inside CUDA-graph
+// capture make no attribute calls.
+int ensure_smem_attr(const void *kernel, int bytes);
 
 #define Q35_CHECK_CUDA(expr)                                   \
   do {                                                         \

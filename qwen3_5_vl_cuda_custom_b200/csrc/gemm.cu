@@ -364,8 +364,7 @@ int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb,
   using L = SmemLayout<BN, STAGES>;
   const int smem = L::bytes(p.E);
   auto kern = gemm_tc_kernel<BN, EPI, STAGES>;
-  Q35_CHECK_CUDA(cudaFuncSetAttribute(
-      kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  { const int _st = ensure_smem_attr(reinterpret_cast<const void *>(kern), smem); if (_st) return _st; }
   const int grid = max(1, min(max_tiles, num_sms()));
   kern<<<grid, kThreads, smem, s>>>(ta, tb, p);
   Q35_LAUNCH_CHECK("gemm_tc launch");
@@ -642,7 +641,7 @@ int launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmPar
                      int max_pair_tiles, cudaStream_t s) {
   const int smem = PairLayout::bytes(p.E);
   auto kern = gemm_pair_kernel<EPI>;
-  Q35_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  { const int _st = ensure_smem_attr(reinterpret_cast<const void *>(kern), smem); if (_st) return _st; }
   const int npairs = max(1, min(max_pair_tiles, num_sms() / 2));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * npairs, 1, 1);

@@ -272,3 +272,43 @@ def test_moe_model_forward_text_only():
     assert torch.isfinite(logits.float()).all()
     assert len(rls) == 2 and rls[0].shape == (16, 32)
     assert step.shape == (2, 1, 512)
+
+
+def test_graphed_layer_replays_eager_forward():
+    """GraphedDecoderLayer (CUDA-graph replay) gives the eager forward's result."""
+    from qwen3_5_vl_cuda_custom_b200 import synthetic as syn
+    from qwen3_5_vl_cuda_custom_b200.configs import tiny_moe_text
+    from qwen3_5_vl_cuda_custom_b200.graphs import GraphedDecoderLayer
+    cfg = tiny_moe_text()
+    g = torch.Generator().manual_seed(21)
+    layer = make_layer(cfg, syn.layer_params(cfg, g))
+    rot = rotary(cfg)
+    pos = syn.text_positions(2, 256).to(DEV)
+    x1 = syn.hidden_states((2, 256, cfg.hidden_size), g).to(DEV, torch.bfloat16)
+    x2 = syn.hidden_states((2, 256, cfg.hidden_size), g).to(DEV, torch.bfloat16)
+    gl = GraphedDecoderLayer(layer, rot, x1, pos)
+    with torch.no_grad():
+        for x in (x1, x2, x1):
+            ref, ref_rl, _ = layer(x, rot.bind(pos))
+            got, got_rl, _ = gl(x)
+            assert torch.equal(got, ref) and torch.equal(got_rl, ref_rl)
+
+
+def test_streamed_runner_copies_in_and_out():
+    from qwen3_5_vl_cuda_custom_b200 import synthetic as syn
+    from qwen3_5_vl_cuda_custom_b200.configs import tiny_moe_text
+    from qwen3_5_vl_cuda_custom_b200.graphs import GraphedDecoderLayer, StreamedLayerRunner
+    cfg = tiny_moe_text()
+    g = torch.Generator().manual_seed(22)
+    layer = make_layer(cfg, syn.layer_params(cfg, g))
+    rot = rotary(cfg)
+    pos = syn.text_positions(1, 256).to(DEV)
+    x = syn.hidden_states((1, 256, cfg.hidden_size), g).to(torch.bfloat16)
+    gl = GraphedDecoderLayer(layer, rot, x.to(DEV), pos)
+    x_host = x.pin_memory()
+    out_host = torch.zeros_like(x_host).pin_memory()
+    StreamedLayerRunner(gl).run(x_host, out_host, 3)
+    torch.cuda.synchronize()
+    with torch.no_grad():
+        ref, _, _ = layer(x.to(DEV), rot.bind(pos))
+    assert torch.equal(out_host, ref.cpu())
