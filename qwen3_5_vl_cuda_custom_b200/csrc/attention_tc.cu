@@ -38,6 +38,25 @@ constexpr int kSmem = 1024 + kBarOff + 16 * 8;
 constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 512;           // O [0,128), S0 [128,256), S1 [256,384)
 
+// Softmax exponentials, split between two pipes: half on the MUFU unit
+// (ex2.approx), half on the FMA pipes.  exp2_fma: x = i + f with i = floor(x),
+// 2^f from a degree-3 polynomial fitted to 2^f on [0, 1) (relative-error
+// least squares on Chebyshev nodes, max relative error 7.8e-5, below the 2^-9
+// rounding P gets when it is packed to bf16), 2^i added to the exponent bits.
+__device__ __forceinline__ float exp2_mufu(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float xc = fmaxf(x, -126.f);
+  const float fi = floorf(xc);
+  const float f = xc - fi;
+  const float p = fmaf(fmaf(fmaf(0.07790717f, f, 0.22623320f), f, 0.69577712f), f, 0.99992782f);
+  const float r = __int_as_float(__float_as_int(p) + (static_cast<int>(fi) << 23));
+  return x < -126.f ? 0.f : r;
+}
+
 struct AttnParams {
   int Hq, Hkv;
   int64_t Sq, Skv;
@@ -250,8 +269,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float a = exp2f(fmaf(s[half * 64 + 2 * i], p.sl2, -mus));
-          const float b2 = exp2f(fmaf(s[half * 64 + 2 * i + 1], p.sl2, -mus));
+          const float a = exp2_mufu(fmaf(s[half * 64 + 2 * i], p.sl2, -mus));
+          const float b2 = exp2_fma(fmaf(s[half * 64 + 2 * i + 1], p.sl2, -mus));
           l += a + b2;
           pk[i] = pack_bf2(a, b2);
         }
@@ -274,6 +293,286 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
           sm100::tmem_ld32(tmem + lane_base + c * 32, r);
+          sm100::tmem_wait_ld();
+          if (valid) {
+#pragma unroll
+            for (int qd = 0; qd < 4; ++qd) {
+              uint4 u;
+              u.x = pack_bf2(__uint_as_float(r[8 * qd + 0]) * inv, __uint_as_float(r[8 * qd + 1]) * inv);
+              u.y = pack_bf2(__uint_as_float(r[8 * qd + 2]) * inv, __uint_as_float(r[8 * qd + 3]) * inv);
+              u.z = pack_bf2(__uint_as_float(r[8 * qd + 4]) * inv, __uint_as_float(r[8 * qd + 5]) * inv);
+              u.w = pack_bf2(__uint_as_float(r[8 * qd + 6]) * inv, __uint_as_float(r[8 * qd + 7]) * inv);
+              reinterpret_cast<uint4 *>(orow + c * 32)[qd] = u;
+            }
+          }
+        }
+      }
+    } else if (valid) {
+      for (int c = 0; c < 16; ++c) reinterpret_cast<uint4 *>(orow)[c] = make_uint4(0, 0, 0, 0);
+    }
+    if (valid && p.lse)
+      p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.Sq + qi] =
+          l > 0.f ? m_used * p.scale + logf(l) : -INFINITY;
+  }
+
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    sm100::tc_fence_after();
+    sm100::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// Two-tile variant (GQA with an even group): one CTA owns the same 128-query
+// block of two heads that share a kv head, so every K/V tile feeds two S
+// MMAs and two PV MMAs.  Two softmax warpgroups (one per head) alternate with
+// the tensor core: while group a exponentiates S_a(j), the MMA warp computes
+// PV_b(j-1) and S_b(j), and vice versa.  TMEM: O_a [0,128), S_a [128,256),
+// O_b [256,384), S_b [384,512).  S is single-buffered per head: S_h(j+1) is
+// issued only after PV_h(j), which reads P_h(j) from the same columns, and
+// tensor operations of one thread complete in issue order, so the commit that
+// announces S_h(j+1) also guarantees PV_h(j) has finished (O_h may then be
+// rescaled without another wait).  Softmax reads S twice from TMEM (row max,
+// then exponentials) to stay within ~200 registers with 10 warps.
+constexpr int kThreads2 = 320;
+constexpr int kQ2Off = 0;                          // Q_a, Q_b: 2 x 2 halves
+constexpr int kK2Off = kQ2Off + 4 * kHalfBytes;    // K: 2 stages x 2 halves
+constexpr int kV2Off = kK2Off + 4 * kHalfBytes;    // V: 2 stages x 2 halves
+constexpr int kBar2Off = kV2Off + 4 * kHalfBytes;
+constexpr int kSmem2 = 1024 + kBar2Off + 16 * 8;
+
+__global__ void __launch_bounds__(kThreads2, 1)
+    attn_tc2_kernel(const __grid_constant__ CUtensorMap tmQ,
+                    const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBar2Off);
+  uint64_t *q_full = bars + 0;
+  uint64_t *kv_full = bars + 1;   // [2]
+  uint64_t *kv_empty = bars + 3;  // [2]
+  uint64_t *s_full = bars + 5;    // [2] per head
+  uint64_t *p_full = bars + 7;    // [2] per head
+  uint64_t *o_done = bars + 9;
+  uint64_t *drain = bars + 10;
+  uint32_t *s_tmem = reinterpret_cast<uint32_t *>(bars + 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // 1-D grid, heaviest query blocks (most causal key tiles) first across all
+  // (batch, head pair) so the tail of the launch is made of short CTAs.
+  const int n_pairs_total = static_cast<int>(gridDim.x) / p.n_mblocks;
+  const int mb = p.n_mblocks - 1 - static_cast<int>(blockIdx.x) / n_pairs_total;
+  const int hp = static_cast<int>(blockIdx.x) % n_pairs_total;  // (b, head pair)
+  const int pairs = p.Hq / 2;
+  const int b = hp / pairs, h0 = (hp % pairs) * 2;
+  const int hk = h0 / (p.Hq / p.Hkv);         // both heads share this kv head
+  const int64_t m0 = static_cast<int64_t>(mb) * kTile;
+  const int64_t diag = p.Skv - p.Sq;
+  int64_t kv_end = p.Skv;
+  if (p.causal) kv_end = min(p.Skv, m0 + kTile + diag);
+  const int n_tiles = kv_end > 0 ? static_cast<int>((kv_end + kTile - 1) / kTile) : 0;
+  const int32_t kv_row = static_cast<int32_t>((static_cast<int64_t>(b) * p.Hkv + hk) * p.Skv);
+
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(&kv_full[i], 1);
+      sm100::mbar_init(&kv_empty[i], 1);
+      sm100::mbar_init(&s_full[i], 1);
+      sm100::mbar_init(&p_full[i], 128);
+    }
+    sm100::mbar_init(o_done, 1);
+    sm100::mbar_init(drain, 1);
+    sm100::fence_mbar_init();
+    sm100::prefetch_tensormap(&tmQ);
+    sm100::prefetch_tensormap(&tmK);
+    sm100::prefetch_tensormap(&tmV);
+  }
+  if (warp == 1) sm100::tmem_alloc(s_tmem, kTmemCols);
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0 && lane == 0 && n_tiles > 0) {
+    // ------------------------------------------------ TMA producer
+    sm100::mbar_arrive_expect_tx(q_full, 4 * kHalfBytes);
+    for (int hh = 0; hh < 2; ++hh) {
+      const int32_t qr = static_cast<int32_t>((static_cast<int64_t>(b) * p.Hq + h0 + hh) * p.Sq + m0);
+      sm100::tma_load_2d(smem + kQ2Off + hh * 2 * kHalfBytes, &tmQ, q_full, 0, qr);
+      sm100::tma_load_2d(smem + kQ2Off + hh * 2 * kHalfBytes + kHalfBytes, &tmQ, q_full, 64, qr);
+    }
+    for (int j = 0; j < n_tiles; ++j) {
+      const int st = j & 1;
+      if (!sm100::mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) {
+        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 321, j, 0);
+        break;
+      }
+      uint8_t *sk = smem + kK2Off + st * 2 * kHalfBytes;
+      uint8_t *sv = smem + kV2Off + st * 2 * kHalfBytes;
+      const int32_t r = kv_row + j * kTile;
+      sm100::mbar_arrive_expect_tx(&kv_full[st], 4 * kHalfBytes);
+      sm100::tma_load_2d(sk, &tmK, &kv_full[st], 0, r);
+      sm100::tma_load_2d(sk + kHalfBytes, &tmK, &kv_full[st], 64, r);
+      sm100::tma_load_2d(sv, &tmV, &kv_full[st], 0, r);
+      sm100::tma_load_2d(sv + kHalfBytes, &tmV, &kv_full[st], 64, r);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc_s = sm100::idesc_bf16_f32(kTile, kTile);
+    constexpr uint32_t idesc_pv = sm100::idesc_bf16_f32(kTile, 128, 0, 1);
+    bool ok = n_tiles > 0;
+    if (ok && !sm100::mbar_wait(q_full, 0)) {
+      report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 322, 0, 0);
+      ok = false;
+    }
+    auto issue_s = [&](int hh, int j) {
+      const int st = j & 1;
+      const uint32_t sq = sm100::smem_u32(smem + kQ2Off + hh * 2 * kHalfBytes);
+      const uint32_t sk = sm100::smem_u32(smem + kK2Off + st * 2 * kHalfBytes);
+      const uint32_t s_tm = tmem + hh * 256 + 128;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * kHalfBytes;
+        const uint64_t ad = sm100::sw128_kmajor_desc(sq + off) + 2 * (kk & 3);
+        const uint64_t bd = sm100::sw128_kmajor_desc(sk + off) + 2 * (kk & 3);
+        sm100::mma_bf16_ss(s_tm, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+      }
+      sm100::mma_commit(&s_full[hh]);
+    };
+    auto issue_pv = [&](int hh, int i) -> bool {
+      if (!sm100::mbar_wait(&p_full[hh], i & 1)) {
+        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 323, i, hh);
+        return false;
+      }
+      sm100::tc_fence_after();
+      const int st = i & 1;
+      const uint32_t sv = sm100::smem_u32(smem + kV2Off + st * 2 * kHalfBytes);
+      const uint32_t o_tm = tmem + hh * 256;
+#pragma unroll
+      for (int kk = 0; kk < kTile / 16; ++kk) {
+        const uint64_t bdesc = sm100::sw128_mnmajor_desc(sv + kk * 2048, kHalfBytes, 1024);
+        sm100::mma_bf16_ts(o_tm, o_tm + 128 + kk * 8, bdesc, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+      }
+      return true;
+    };
+    for (int j = 0; j < n_tiles && ok; ++j) {
+      const int st = j & 1;
+      if (!sm100::mbar_wait(&kv_full[st], (j >> 1) & 1)) {
+        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 324, j, 0);
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      if (j > 0 && !issue_pv(0, j - 1)) { ok = false; break; }
+      issue_s(0, j);
+      if (j > 0) {
+        if (!issue_pv(1, j - 1)) { ok = false; break; }
+        sm100::mma_commit(&kv_empty[(j - 1) & 1]);
+      }
+      issue_s(1, j);
+    }
+    if (ok) {
+      if (issue_pv(0, n_tiles - 1) && issue_pv(1, n_tiles - 1)) {
+        sm100::mma_commit(&kv_empty[(n_tiles - 1) & 1]);
+        sm100::mma_commit(o_done);
+      }
+    }
+    sm100::mma_commit(drain);
+    if (!sm100::mbar_wait(drain, 0)) report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 325, 0, 0);
+  } else if (warp >= 2) {
+    // ------------------------------------------------ softmax, one group per head
+    const int hh = (warp - 2) >> 2;          // warps 2-5: head a, 6-9: head b
+    const int q = warp & 3;                  // TMEM lane quadrant of this warp
+    const int row = q * 32 + lane;
+    const int64_t qi = m0 + row;
+    const int h = h0 + hh;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t o_tm = tmem + lane_base + hh * 256;
+    const uint32_t s_tm = o_tm + 128;
+    const int64_t lim_c = p.causal ? min(qi + diag, p.Skv - 1) : p.Skv - 1;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!sm100::mbar_wait(&s_full[hh], j & 1)) {
+        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 326, j, row);
+        ok = false;
+        break;
+      }
+      sm100::tc_fence_after();
+      const int64_t n0 = static_cast<int64_t>(j) * kTile;
+      const bool masked = n0 + kTile - 1 > lim_c;
+      // the whole score row in two 64-column loads, one wait
+      uint32_t sr[kTile];
+      sm100::tmem_ld64(s_tm, sr);
+      sm100::tmem_ld64(s_tm + 64, sr + 64);
+      sm100::tmem_wait_ld();
+      if (masked) {
+#pragma unroll
+        for (int c = 0; c < kTile; ++c)
+          if (n0 + c > lim_c) sr[c] = __float_as_uint(-INFINITY);
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < kTile; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      const float m_new = fmaxf(m_used, mx);
+      bool need = false;
+      float alpha = 1.f;
+      if (j == 0 || m_used == -INFINITY) {
+        m_used = m_new;
+      } else if ((m_new - m_used) * p.sl2 > 8.f) {
+        need = true;
+        alpha = exp2f((m_used - m_new) * p.sl2);
+        m_used = m_new;
+        l *= alpha;
+      }
+      const float mus = ((m_used == -INFINITY) ? 0.f : m_used) * p.sl2;
+      // PV(j-1) is complete (it precedes S(j) in the tensor pipe): O may be scaled.
+      if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld32(o_tm + c * 32, r);
+          sm100::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          sm100::tmem_st32(o_tm + c * 32, r);
+        }
+      }
+      // exponentials, bf16 P over the first 64 S columns
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float a = exp2_mufu(fmaf(__uint_as_float(sr[half * 64 + 2 * i]), p.sl2, -mus));
+          const float b2 = exp2_fma(fmaf(__uint_as_float(sr[half * 64 + 2 * i + 1]), p.sl2, -mus));
+          l += a + b2;
+          pk[i] = pack_bf2(a, b2);
+        }
+        sm100::tmem_st32(s_tm + half * 32, pk);
+      }
+      sm100::tmem_wait_st();
+      sm100::tc_fence_before();
+      sm100::mbar_arrive(&p_full[hh]);
+    }
+    // ---- epilogue: O / l -> bf16, out[b, qi, h*128 + d]
+    const bool valid = qi < p.Sq;
+    uint16_t *orow = p.out + ((static_cast<int64_t>(b) * p.Sq + qi) * p.Hq + h) * 128;
+    if (n_tiles > 0 && ok) {
+      if (!sm100::mbar_wait(o_done, 0)) {
+        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 327, n_tiles, row);
+      } else {
+        sm100::tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          sm100::tmem_ld32(o_tm + c * 32, r);
           sm100::tmem_wait_ld();
           if (valid) {
 #pragma unroll
@@ -340,6 +639,14 @@ int q35_attn_prefill_tc(const void *q, const void *k, const void *v, void *out,
   p.out = static_cast<uint16_t *>(out);
   p.lse = lse;
   p.err = err;
+  if ((Hq / Hkv) % 2 == 0) {
+    // GQA with an even group: two heads per CTA share each K/V tile.
+    { const int _st = ensure_smem_attr(reinterpret_cast<const void *>(attn_tc2_kernel), kSmem2); if (_st) return _st; }
+    dim3 grid2(static_cast<unsigned>(p.n_mblocks * B * Hq / 2));
+    attn_tc2_kernel<<<grid2, kThreads2, kSmem2, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+    Q35_LAUNCH_CHECK("attn_prefill_tc2 launch");
+    return Q35_OK;
+  }
   { const int _st = ensure_smem_attr(reinterpret_cast<const void *>(attn_tc_kernel), kSmem); if (_st) return _st; }
   dim3 grid(p.n_mblocks, static_cast<unsigned>(B * Hq));
   attn_tc_kernel<<<grid, kThreads, kSmem, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
