@@ -12,9 +12,11 @@ inputs (synthetic: no checkpoint or dataset).
 (qwen3_5_vl_cuda_custom_b200.graphs.GraphedDecoderLayer); the eager module
 call is reported beside it.
 
-One process per GPU (torchrun for N > 1).  Each rank runs the full layer on
-its own 4096-token sequence (data-parallel over sequences, experts
-replicated: "replicas"), so per-GPU work is fixed ("scaling": "weak").
+One process per GPU (torchrun for N > 1).  Each rank prefills its own
+4096-token sequence (attention data-parallel over sequences) and the experts
+are sharded expert-parallel, 128/N per GPU, with NCCL all-to-all dispatch and
+return (qwen3_5_vl_cuda_custom_b200.ep); per-GPU work is fixed ("scaling":
+"weak").
 A step is one layer forward; the L2 is flushed (256 MiB write) between
 steps outside the timed events.  ``value`` is whole-job tokens/s from
 per-step CUDA events (max over ranks); ``e2e`` re-times the same step through
@@ -38,6 +40,7 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+LINK_GBS = 770.0  # measured NVLink peer copy per direction on this pool
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -110,7 +113,7 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- workload
-def build_layer(cfg, seed: int, device):
+def build_layer(cfg, seed: int, device, expert_group=None):
     from qwen3_5_vl_cuda_custom_b200 import synthetic as syn
     from qwen3_5_vl_cuda_custom_b200.modules import CudaTextDecoderLayer, TextMRoPE
     g = torch.Generator().manual_seed(seed)
@@ -118,8 +121,9 @@ def build_layer(cfg, seed: int, device):
     layer = CudaTextDecoderLayer(cfg.hidden_size, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
                                  cfg.intermediate_size, cfg.rms_norm_eps, use_moe=True,
                                  num_experts=cfg.num_experts, top_k=cfg.num_experts_per_tok,
-                                 moe_intermediate_size=cfg.moe_intermediate_size)
-    layer.load_state_dict(P)
+                                 moe_intermediate_size=cfg.moe_intermediate_size,
+                                 expert_group=expert_group)
+    layer.load_state_dict(P)  # expert-parallel layers keep their slice of the experts
     layer = layer.to(device, torch.bfloat16)
     rot = TextMRoPE(cfg.head_dim, cfg.rope_theta, cfg.mrope_section).to(device)
     return layer, rot, P, g
@@ -143,6 +147,9 @@ def stage_table(cfg, T: int, S: int) -> dict:
         "gate_up_swiglu": ("tensor", T * k * 2 * H * 2 * I),
         "down": ("tensor", T * k * 2 * I * H),
         "combine_residual": ("hbm", T * k * H * 2 + 2 * T * H * 2 + T * k * 4),
+        # expert parallelism: rows leaving for other ranks, each direction
+        "ep_dispatch": ("link", T * k * H * 2),
+        "ep_return": ("link", T * k * H * 2),
     }
 
 
@@ -180,13 +187,26 @@ def staged_forward(layer, rot, x, pos, marks=None):
     mark("router")
     perm = K.moe_permute(idx, moe.num_experts)
     mark("permute")
-    gu_p, dn_p = moe._packed_experts()
     xs = K.gather_rows(m2, perm.sorted_tok)
     mark("gather")
-    act = K.grouped_gateup_swiglu(xs, moe.gate_up_proj, perm, w_packed=gu_p)
-    mark("gate_up_swiglu")
-    y = K.grouped_down(act, moe.down_proj, perm, w_packed=dn_p)
-    mark("down")
+    exchange = getattr(moe, "exchange", None)
+    if exchange is not None:  # expert parallel: rows travel to the expert owners
+        from qwen3_5_vl_cuda_custom_b200.ep import _local_permutation
+        em, st = exchange.dispatch(xs, perm.counts)
+        mark("ep_dispatch")
+        local = _local_permutation(st.local_offsets, st.local_counts)
+        act = K.grouped_gateup_swiglu(em, moe.gate_up_proj, local)
+        mark("gate_up_swiglu")
+        y_em = K.grouped_down(act, moe.down_proj, local)
+        mark("down")
+        y = exchange.combine(y_em, st)
+        mark("ep_return")
+    else:
+        gu_p, dn_p = moe._packed_experts()
+        act = K.grouped_gateup_swiglu(xs, moe.gate_up_proj, perm, w_packed=gu_p)
+        mark("gate_up_swiglu")
+        y = K.grouped_down(act, moe.down_proj, perm, w_packed=dn_p)
+        mark("down")
     out = K.moe_combine(y, wts, perm.slot_pos, h.reshape(-1, H), B * S, H)
     mark("combine_residual")
     return out.reshape(B, S, H)
@@ -308,7 +328,13 @@ def run_ours(args, world, rank, local):
     cfg = a3b_moe_text(1)
     S = args.tokens
     T = S
-    layer, rot, P, g = build_layer(cfg, 1, dev)
+    ep_group = None
+    if world > 1:
+        import torch.distributed as dist
+        ep_group = dist.group.WORLD
+    layer, rot, P, g = build_layer(cfg, 1, dev, ep_group)
+    if world > 1:  # each rank prefills its own sequence
+        g = torch.Generator().manual_seed(1000 + rank)
     x_cpu = syn.hidden_states((1, S, cfg.hidden_size), g)
     x = x_cpu.to(dev, torch.bfloat16)
     pos_cpu = syn.text_positions(1, S)
@@ -353,25 +379,36 @@ def run_ours(args, world, rank, local):
                 samples.setdefault(name, []).append(a.elapsed_time(b))
         stage_ms = {k: statistics.median(v) for k, v in samples.items()}
 
-        graphed = GraphedDecoderLayer(layer, rot, x, pos)
-        total_ms = timed(graphed.replay)
+        if world == 1:
+            graphed = GraphedDecoderLayer(layer, rot, x, pos)
+            total_ms = timed(graphed.replay)
+        else:  # expert-parallel exchange sizes come from the host: not capturable
+            graphed = None
+            total_ms = eager_ms
         ms_per_step = total_ms / args.steps
         value = world * T * args.steps / (total_ms / 1e3)
         eager_value = world * T * args.steps / (eager_ms / 1e3)
 
-        # ---------------- end to end through the public API: StreamedLayerRunner
-        # copies each step's input from pinned host memory and its output back,
-        # overlapping the copies with the neighbouring steps' replays
-        from qwen3_5_vl_cuda_custom_b200.graphs import StreamedLayerRunner
+        # ---------------- end to end through the public API: each step copies its
+        # input from pinned host memory and its output back.  One GPU: the
+        # StreamedLayerRunner overlaps the copies with neighbouring replays.
         x_host = x_cpu.to(torch.bfloat16).pin_memory()
         out_host = torch.empty_like(x_host).pin_memory()
-        runner = StreamedLayerRunner(graphed)
-        runner.run(x_host, out_host, 2)
+        if graphed is not None:
+            from qwen3_5_vl_cuda_custom_b200.graphs import StreamedLayerRunner
+            runner = StreamedLayerRunner(graphed)
+            run_e2e = lambda n: runner.run(x_host, out_host, n)  # noqa: E731
+        else:
+            def run_e2e(n):
+                for _ in range(n):
+                    y, _, _ = layer(x_host.to(dev, non_blocking=True), bpos)
+                    out_host.copy_(y, non_blocking=True)
+        run_e2e(2)
         barrier(world)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        runner.run(x_host, out_host, args.steps)
+        run_e2e(args.steps)
         e1.record()
         barrier(world)
         e2e_ms = allreduce_max(e0.elapsed_time(e1), world)
@@ -388,6 +425,10 @@ def run_ours(args, world, rank, local):
         achieved = amount / t_top / 1e12
         peak = peaks["bf16_tflops"]
         unit = "TFLOP/s"
+    elif bound == "link":
+        achieved = amount * (world - 1) / world / t_top / 1e9
+        peak = LINK_GBS
+        unit = "GB/s"
     else:
         achieved = amount / t_top / 1e9
         peak = peaks["hbm_gbs"]
@@ -395,8 +436,10 @@ def run_ours(args, world, rank, local):
     breakdown = {}
     for name, ms in stage_ms.items():
         b, a = table[name]
+        if b == "link":
+            a = a * (world - 1) / world
         rate = a / (ms / 1e3) / (1e12 if b == "tensor" else 1e9)
-        pk = peaks["bf16_tflops"] if b == "tensor" else peaks["hbm_gbs"]
+        pk = {"tensor": peaks["bf16_tflops"], "link": LINK_GBS}.get(b, peaks["hbm_gbs"])
         breakdown[name] = {"ms": round(ms, 4), "bound": b,
                            "achieved": round(rate, 1), "frac": round(rate / pk, 3)}
 
@@ -428,7 +471,10 @@ def run_ours(args, world, rank, local):
                    "hidden": cfg.hidden_size, "heads": f"{cfg.num_heads}/{cfg.num_kv_heads}x{cfg.head_dim}",
                    "experts": f"{cfg.num_experts} top-{cfg.num_experts_per_tok} I={cfg.moe_intermediate_size}",
                    "tokens_per_gpu": T, "global_batch": world, "seq_len": S,
-                   "parallelism": f"dp{world} sequences, experts replicated",
+                   "parallelism": (f"ep{world}: {cfg.num_experts // world} experts/GPU, NCCL "
+                                   f"all-to-all; dp{world} attention over sequences"
+                                   if world > 1 else "1 GPU, all experts local"),
+                   "mode": "CUDA-graph replay" if world == 1 else "eager (host-sized all-to-all)",
                    "l2": "256 MiB flush between timed steps"},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": in_bytes,
                 "d2h_bytes_per_step": in_bytes,

@@ -26,7 +26,9 @@ def _layer_uses_moe(cfg: MoETextConfig, layer_idx: int) -> bool:
 
 
 class CudaQwen3VLMoeModel(nn.Module):
-    def __init__(self, cfg: Qwen3VLConfig) -> None:
+    def __init__(self, cfg: Qwen3VLConfig, expert_group=None) -> None:
+        """``expert_group`` shards every MoE layer's experts over that process
+        group (expert parallelism); attention and the rest stay replicated."""
         super().__init__()
         if cfg.family != "moe" or not isinstance(cfg.text, MoETextConfig):
             raise ValueError(f"expected an MoE config, got {cfg.family}")
@@ -41,7 +43,8 @@ class CudaQwen3VLMoeModel(nn.Module):
                 head_dim=t.head_dim, intermediate_size=t.intermediate_size,
                 rms_norm_eps=t.rms_norm_eps, use_moe=_layer_uses_moe(t, i),
                 num_experts=t.num_experts, top_k=t.num_experts_per_tok,
-                moe_intermediate_size=t.moe_intermediate_size, attention_bias=t.attention_bias)
+                moe_intermediate_size=t.moe_intermediate_size, attention_bias=t.attention_bias,
+                expert_group=expert_group)
             for i in range(t.num_layers)
         ])
         self.norm = CudaRMSNorm(t.hidden_size, eps=t.rms_norm_eps)
