@@ -129,7 +129,7 @@ def build_layer(cfg, seed: int, device, expert_group=None):
     return layer, rot, P, g
 
 
-def stage_table(cfg, T: int, S: int) -> dict:
+def stage_table(cfg, T: int, S: int, world: int = 1) -> dict:
     """Algorithmic work per stage: (bound, amount) with FLOPs or bytes."""
     H, D, Hq, Hkv = cfg.hidden_size, cfg.head_dim, cfg.num_heads, cfg.num_kv_heads
     E, k, I = cfg.num_experts, cfg.num_experts_per_tok, cfg.moe_intermediate_size
@@ -147,9 +147,10 @@ def stage_table(cfg, T: int, S: int) -> dict:
         "gate_up_swiglu": ("tensor", T * k * 2 * H * 2 * I),
         "down": ("tensor", T * k * 2 * I * H),
         "combine_residual": ("hbm", T * k * H * 2 + 2 * T * H * 2 + T * k * 4),
-        # expert parallelism: rows leaving for other ranks, each direction
-        "ep_dispatch": ("link", T * k * H * 2),
-        "ep_return": ("link", T * k * H * 2),
+        # expert parallelism: one row per (token, destination rank), each
+        # direction; expected ranks per token N(1 - (1 - 1/N)^k), N = world
+        "ep_dispatch": ("link", T * H * 2 * world * (1 - (1 - 1 / world) ** k)),
+        "ep_return": ("link", T * H * 2 * world * (1 - (1 - 1 / world) ** k)),
     }
 
 
@@ -187,26 +188,17 @@ def staged_forward(layer, rot, x, pos, marks=None):
     mark("router")
     perm = K.moe_permute(idx, moe.num_experts)
     mark("permute")
+    if getattr(moe, "exchange", None) is not None:  # expert parallel
+        out = moe.experts(m2, idx, wts, h.reshape(-1, H), mark=mark)
+        mark("combine_residual")
+        return out.reshape(B, S, H)
     xs = K.gather_rows(m2, perm.sorted_tok)
     mark("gather")
-    exchange = getattr(moe, "exchange", None)
-    if exchange is not None:  # expert parallel: rows travel to the expert owners
-        from qwen3_5_vl_cuda_custom_b200.ep import _local_permutation
-        em, st = exchange.dispatch(xs, perm.counts)
-        mark("ep_dispatch")
-        local = _local_permutation(st.local_offsets, st.local_counts)
-        act = K.grouped_gateup_swiglu(em, moe.gate_up_proj, local)
-        mark("gate_up_swiglu")
-        y_em = K.grouped_down(act, moe.down_proj, local)
-        mark("down")
-        y = exchange.combine(y_em, st)
-        mark("ep_return")
-    else:
-        gu_p, dn_p = moe._packed_experts()
-        act = K.grouped_gateup_swiglu(xs, moe.gate_up_proj, perm, w_packed=gu_p)
-        mark("gate_up_swiglu")
-        y = K.grouped_down(act, moe.down_proj, perm, w_packed=dn_p)
-        mark("down")
+    gu_p, dn_p = moe._packed_experts()
+    act = K.grouped_gateup_swiglu(xs, moe.gate_up_proj, perm, w_packed=gu_p)
+    mark("gate_up_swiglu")
+    y = K.grouped_down(act, moe.down_proj, perm, w_packed=dn_p)
+    mark("down")
     out = K.moe_combine(y, wts, perm.slot_pos, h.reshape(-1, H), B * S, H)
     mark("combine_residual")
     return out.reshape(B, S, H)
@@ -417,7 +409,7 @@ def run_ours(args, world, rank, local):
     K.device_error_check()
 
     peaks, peak_src = load_peaks()
-    table = stage_table(cfg, T, S)
+    table = stage_table(cfg, T, S, world)
     top = max(stage_ms, key=stage_ms.get)
     bound, amount = table[top]
     t_top = stage_ms[top] / 1e3

@@ -158,8 +158,9 @@ Q35_API int q35_topk_fwd(const float *x, float *vals, int64_t *idx, int64_t rows
  *   tile_offsets int32 [E+1]   prefix sum of ceil(counts[e] / 128), the
  *                               grouped-GEMM M-tile schedule
  * workspace: int32 scratch of q35_moe_permute_workspace(T, E) elements.
- * Expert ids outside [0, E) are recorded in the device error word and the
- * pair is dropped (slot_pos = -1).                                        */
+ * A negative id marks an empty slot (slot_pos = -1, no error: the
+ * expert-parallel receiver uses it); ids >= E are recorded in the device
+ * error word and the pair is dropped (slot_pos = -1).                      */
 Q35_API int64_t q35_moe_permute_workspace(int64_t T, int E);
 Q35_API int q35_moe_permute(const int32_t *idx, int64_t T, int k, int E,
                     int32_t *counts, int32_t *offsets, int32_t *sorted_tok,
@@ -185,6 +186,19 @@ Q35_API int q35_moe_permute_noalloc(const int32_t *idx, int64_t T, int k, int E,
                                     int32_t *counts, int32_t *offsets,
                                     int32_t *sorted_tok, int32_t *slot_pos,
                                     int32_t *tile_offsets, q35_stream_t stream);
+
+/* Expert-parallel send slabs.  A token sends at most one row to each rank,
+ * so the send buffer send bf16 [N, T, H] has a fixed slab of T rows per
+ * destination: row (d, t) = x[t] if one of token t's top-k experts
+ * (idx int32 [T, k], global ids) is owned by rank d (experts
+ * [d*El, (d+1)*El)), else left untouched.  meta_idx int32 [N, T, k] holds, at
+ * slot j, the slot's expert id local to rank d or -1, meta_w fp32 [N, T, k]
+ * its weight (w fp32 [T, k]) or 0; ret_pos int32 [T, N] = d*T + t for the
+ * ranks token t uses, else -1.  k <= 16, N <= 32.  An even-split all-to-all
+ * of these slabs needs no host-side sizes.  No reference counterpart.       */
+Q35_API int q35_ep_scatter(const void *x, const int32_t *idx, const float *w, int64_t T, int k,
+                           int64_t H, int El, int N, void *send, int32_t *meta_idx,
+                           float *meta_w, int32_t *ret_pos, q35_stream_t stream);
 
 /* dst[r,:] = src[rows[r],:] for r < n (bf16, cols % 8 == 0); n may be read
  * from device memory (n_dev != NULL: *n_dev rows, at most n_max).           */

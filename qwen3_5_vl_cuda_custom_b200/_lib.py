@@ -42,6 +42,8 @@ _SIGS = {
     "q35_moe_permute_noalloc_max_workspace": (c_int64, []),
     "q35_moe_permute_noalloc": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_void_p, c_void_p]),
+    "q35_ep_scatter": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_int, c_int,
+                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "q35_gather_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p]),
     "q35_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                               c_int64, c_void_p]),

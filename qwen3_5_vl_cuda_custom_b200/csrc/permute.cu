@@ -34,7 +34,8 @@ __device__ __forceinline__ void build_masks(const int32_t *__restrict__ idx,
   if (t < T) {
     for (int j = 0; j < k; ++j) {
       const int e = idx[t * k + j];
-      if (e < 0 || e >= E) {
+      if (e < 0) continue;  // empty slot (expert-parallel receive side)
+      if (e >= E) {
         report_error(err, DEV_ERR_INDEX, 101, static_cast<int>(t), e);
         continue;
       }
@@ -460,5 +461,71 @@ extern "C" int q35_moe_permute_noalloc(const int32_t *idx, int64_t T, int k,
         idx, T, k, E, scratch, offsets, sorted_tok, slot_pos, nullptr);
     Q35_LAUNCH_CHECK("permute_noalloc scatter launch");
   }
+  return Q35_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Expert-parallel send slabs.  Each token sends at most one row to each rank
+// (the rank that owns one or more of its top-k experts), so a fixed slab of
+// T rows per destination holds every possible send: row (d, t) of the send
+// buffer is token t's hidden row if token t uses an expert of rank d.  Its
+// slot list meta_idx[(d, t), j] is the slot's expert id local to rank d, or -1
+// for slots of other ranks (and for every slot of an unused row); meta_w the
+// routing weights.  ret_pos[t, d] = d*T + t if token t uses rank d, else -1:
+// where rank d's partial sum for token t comes back.  One CTA per token.
+namespace q35 {
+namespace {
+__global__ void __launch_bounds__(256) ep_scatter_kernel(
+    const uint16_t *__restrict__ x, const int32_t *__restrict__ idx, const float *__restrict__ w,
+    int64_t T, int k, int64_t H, int El, int N, uint16_t *__restrict__ send,
+    int32_t *__restrict__ meta_idx, float *__restrict__ meta_w, int32_t *__restrict__ ret_pos) {
+  const int64_t t = blockIdx.x;
+  __shared__ int s_e[16];
+  __shared__ uint32_t s_used;  // bit d: token t sends to rank d (N <= 32)
+  if (threadIdx.x == 0) s_used = 0;
+  __syncthreads();
+  if (threadIdx.x < k) {
+    const int e = idx[t * k + threadIdx.x];
+    s_e[threadIdx.x] = e;
+    if (e >= 0 && e / El < N) atomicOr(&s_used, 1u << (e / El));
+  }
+  __syncthreads();
+  const uint32_t used = s_used;
+  // slot lists and return positions
+  for (int i = threadIdx.x; i < N * k; i += blockDim.x) {
+    const int d = i / k, j = i % k;
+    const int e = s_e[j];
+    const int64_t row = static_cast<int64_t>(d) * T + t;
+    const bool mine = e >= 0 && e / El == d;
+    meta_idx[row * k + j] = mine ? e - d * El : -1;
+    meta_w[row * k + j] = mine ? w[t * k + j] : 0.f;
+  }
+  for (int d = threadIdx.x; d < N; d += blockDim.x)
+    ret_pos[t * N + d] = ((used >> d) & 1u) ? static_cast<int32_t>(d * T + t) : -1;
+  // token row into each used slab
+  const uint4 *src = reinterpret_cast<const uint4 *>(x + t * H);
+  for (int d = 0; d < N; ++d) {
+    if (!((used >> d) & 1u)) continue;
+    uint4 *dst = reinterpret_cast<uint4 *>(send + (static_cast<int64_t>(d) * T + t) * H);
+    for (int64_t c = threadIdx.x; c < H / 8; c += blockDim.x) dst[c] = src[c];
+  }
+}
+}  // namespace
+}  // namespace q35
+
+extern "C" int q35_ep_scatter(const void *x, const int32_t *idx, const float *w, int64_t T,
+                              int k, int64_t H, int El, int N, void *send, int32_t *meta_idx,
+                              float *meta_w, int32_t *ret_pos, q35_stream_t stream) {
+  if (!send || !meta_idx || !meta_w || !ret_pos || (T > 0 && (!x || !idx || !w)))
+    return fail(Q35_ERR_INVALID, "ep_scatter: null pointer");
+  if (T < 0 || k < 1 || k > 16 || El < 1 || N < 1 || N > 32 || H <= 0 || H % 8 != 0)
+    return fail(Q35_ERR_SHAPE, "ep_scatter: k %d (<=16) N %d (<=32) H %lld (x8)", k, N,
+                (long long)H);
+  if (!aligned16(x) || !aligned16(send)) return fail(Q35_ERR_ALIGN, "ep_scatter: alignment");
+  if (T == 0) return Q35_OK;
+  ep_scatter_kernel<<<static_cast<unsigned>(T), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t *>(x), idx, w, T, k, H, El, N, static_cast<uint16_t *>(send),
+      meta_idx, meta_w, ret_pos);
+  Q35_LAUNCH_CHECK("ep_scatter launch");
   return Q35_OK;
 }

@@ -1,32 +1,29 @@
-"""Expert parallelism: token dispatch to the rank that owns each expert, and the
-way back, over torch.distributed all-to-all (NCCL over NVLink on GPUs).
+"""Expert parallelism: token dispatch to the ranks that own a token's experts,
+and the way back, over torch.distributed all-to-all (NCCL over NVLink on GPUs).
 
-Rank r of an N-rank group owns experts [r * E/N, (r + 1) * E/N).  The
-single-GPU MoE pipeline already sorts the routed (token, slot) pairs by
-(expert, token) and gathers their rows in that order, so the rows bound for
-each owner rank are contiguous: they are the send buffer as they stand.
+Rank r of an N-rank group owns experts [r * E/N, (r + 1) * E/N).  A token
+whose top-k experts sit on several ranks is sent once to each of those ranks
+(not once per expert) with a k-slot list of (local expert id, routing weight).
+A token sends at most one row to a rank, so every send fits a fixed slab of T
+rows per destination: the all-to-alls split evenly and need no host-side
+sizes (no host synchronisation; the layer can be captured in a CUDA graph).
 
-dispatch():
-  1. all_to_all of the per-expert row counts (int32, E/N per destination);
-     the counts come to the host once to size the row exchange,
-  2. all_to_all of the rows (bf16, H per row),
-  3. received rows are source-major (rank s, then expert, then token); one row
-     gather makes them expert-major (expert, then source rank, then token), the
-     layout the grouped GEMM reads, with per-local-expert offsets.
-combine():
-  the inverse gather back to source-major, then the reverse all_to_all; the
-  rows land in the sender's sorted order, where the single-GPU combine kernel
-  (weights, residual) consumes them unchanged.
+Sender:   q35_ep_scatter writes token t's row and slot list into slab d for
+          each rank d it uses (slot id -1: not this rank's expert).
+Receiver: the N*T received slot lists (-1 = empty slot, unused rows are all
+          -1) go through the (expert, token) permutation; the gather, grouped
+          gate_up/SwiGLU, grouped down and weighted combine kernels run on
+          them unchanged, leaving one bf16 partial sum per received row.
+Return:   the reverse all-to-all brings each rank's partial sums back; the
+          combine kernel adds a token's partials (weight 1, ret_pos) and its
+          residual.
 
-The row gathers are this library's gather kernel on CUDA tensors; the index
-bookkeeping (a few small int tensors) is plain torch on the same device.  The
-reference has no counterpart: it runs every expert on one GPU
-(REF cuda_qwen3_vl/modules/moe.py:71-83).
+Link traffic is (N-1) * T rows each way per rank whether a slab row is used
+or not (at most ~1/(1-(1-1/N)^k) above the rows actually needed: 1.0x at
+N = 2, 1.5x at N = 8 with k = 8).  The reference has no counterpart: it runs
+every expert on one GPU (REF cuda_qwen3_vl/modules/moe.py:71-83).
 """
 from __future__ import annotations
-
-from dataclasses import dataclass
-from typing import Callable
 
 import torch
 import torch.distributed as dist
@@ -35,27 +32,10 @@ from . import kernels as K
 from .modules import CudaSparseMoE
 
 
-@dataclass
-class DispatchState:
-    send_splits: list[int]          # rows sent to each rank
-    recv_splits: list[int]          # rows received from each rank
-    order: torch.Tensor             # expert-major row r <- source-major row order[r]
-    inverse: torch.Tensor           # source-major row r <- expert-major row inverse[r]
-    local_offsets: torch.Tensor     # int32 [E_local + 1] offsets of the expert-major rows
-    local_counts: torch.Tensor      # int32 [E_local]
-
-
-def _default_gather(src: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
-    if src.is_cuda:
-        return K.gather_rows(src, rows.to(torch.int32))
-    return src.index_select(0, rows.long())
-
-
 class ExpertParallelExchange:
-    """All-to-all dispatch/combine of expert-sorted rows within ``group``."""
+    """Even-split all-to-all between the ranks of ``group``."""
 
-    def __init__(self, num_experts: int, group=None,
-                 gather: Callable[[torch.Tensor, torch.Tensor], torch.Tensor] | None = None):
+    def __init__(self, num_experts: int, group=None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -63,71 +43,16 @@ class ExpertParallelExchange:
             raise ValueError(f"{num_experts} experts do not split over {self.world} ranks")
         self.E = num_experts
         self.E_local = num_experts // self.world
-        self.gather = gather or _default_gather
 
     @property
     def expert_range(self) -> tuple[int, int]:
         return self.rank * self.E_local, (self.rank + 1) * self.E_local
 
-    def dispatch(self, rows: torch.Tensor, expert_counts: torch.Tensor):
-        """rows: [R, H] sorted by (expert, token); expert_counts: int [E] rows per
-        expert.  Returns (expert-major received rows [R_recv, H], state)."""
-        N, El = self.world, self.E_local
-        dev = rows.device
-        counts = expert_counts.to(torch.int32).reshape(N, El).contiguous()
-        recv_counts = torch.empty_like(counts)
-        dist.all_to_all_single(recv_counts, counts, group=self.group)
-        both = torch.stack([counts.sum(1), recv_counts.sum(1)]).cpu()
-        send_splits = both[0].tolist()
-        recv_splits = both[1].tolist()
-        recv = rows.new_empty(sum(recv_splits), rows.shape[1])
-        dist.all_to_all_single(recv, rows.contiguous(), recv_splits, send_splits, group=self.group)
-
-        # source-major (s, e) blocks -> expert-major (e, s) blocks
-        c = recv_counts.to(torch.int64)                          # [N, El]
-        src_start = (torch.cumsum(c.reshape(-1), 0) - c.reshape(-1)).reshape(N, El)
-        sizes_em = c.t().reshape(-1)                             # (e, s) order
-        total = int(sum(recv_splits))
-        block_src = src_start.t().reshape(-1)
-        dst_start = torch.cumsum(sizes_em, 0) - sizes_em
-        ar = torch.arange(total, device=dev, dtype=torch.int64)
-        order = (torch.repeat_interleave(block_src, sizes_em, output_size=total)
-                 + ar - torch.repeat_interleave(dst_start, sizes_em, output_size=total))
-        inverse = torch.empty_like(order)
-        inverse[order] = ar
-        local_counts = c.sum(0).to(torch.int32)
-        local_offsets = torch.zeros(El + 1, device=dev, dtype=torch.int32)
-        local_offsets[1:] = torch.cumsum(local_counts, 0)
-        em_rows = self.gather(recv, order) if total else recv
-        state = DispatchState(send_splits, recv_splits, order.to(torch.int32),
-                              inverse.to(torch.int32), local_offsets, local_counts)
-        return em_rows, state
-
-    def combine(self, y_expert_major: torch.Tensor, state: DispatchState) -> torch.Tensor:
-        """Expert outputs (expert-major, as dispatched) back to the sender's sorted rows."""
-        src_major = (self.gather(y_expert_major, state.inverse) if y_expert_major.shape[0]
-                     else y_expert_major)
-        out = y_expert_major.new_empty(sum(state.send_splits), y_expert_major.shape[1])
-        dist.all_to_all_single(out, src_major.contiguous(), state.send_splits, state.recv_splits,
-                               group=self.group)
+    def exchange(self, buf: torch.Tensor) -> torch.Tensor:
+        """buf [N * rows, ...]: slab d goes to rank d; returns the N received slabs."""
+        out = torch.empty_like(buf)
+        dist.all_to_all_single(out, buf.contiguous(), group=self.group)
         return out
-
-
-def _local_permutation(offsets: torch.Tensor, counts: torch.Tensor):
-    """A kernels.Permutation over the expert-major received rows (the grouped
-    GEMM reads offsets; the 128-row tile prefix is rebuilt for completeness)."""
-    tiles = (counts.to(torch.int64) + 127) // 128
-    tile_offsets = torch.zeros_like(offsets)
-    tile_offsets[1:] = torch.cumsum(tiles, 0).to(torch.int32)
-    return K.Permutation(counts, offsets, None, None, tile_offsets, counts.numel())
-
-
-def make_expert_parallel_moe(hidden_size: int, moe_intermediate_size: int, num_experts: int,
-                             top_k: int, norm_topk_prob: bool = True, group=None):
-    """CudaSparseMoE whose experts are sharded over ``group`` (see
-    ExpertParallelSparseMoE)."""
-    return ExpertParallelSparseMoE(hidden_size, moe_intermediate_size, num_experts, top_k,
-                                   norm_topk_prob, group=group)
 
 
 class ExpertParallelSparseMoE(CudaSparseMoE):
@@ -161,13 +86,39 @@ class ExpertParallelSparseMoE(CudaSparseMoE):
         super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
 
     def experts(self, x2d: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor,
-                residual: torch.Tensor | None = None) -> torch.Tensor:
+                residual: torch.Tensor | None = None, mark=None) -> torch.Tensor:
+        """``mark(name)`` (optional) is called after each stage (benchmark timing)."""
+        mark = mark or (lambda name: None)
         T, H = x2d.shape
-        perm = K.moe_permute(idx, self.num_experts)
-        xs = K.gather_rows(x2d, perm.sorted_tok)
-        em, st = self.exchange.dispatch(xs, perm.counts)
-        local = _local_permutation(st.local_offsets, st.local_counts)
-        act = K.grouped_gateup_swiglu(em, self.gate_up_proj, local)
-        y_em = K.grouped_down(act, self.down_proj, local)
-        y = self.exchange.combine(y_em, st)
-        return K.moe_combine(y, weights, perm.slot_pos, residual, T, H)
+        k = idx.shape[1]
+        ex = self.exchange
+        N, El = ex.world, ex.E_local
+        dev = x2d.device
+        # ---- sender: slab d holds the rows and slot lists for rank d
+        send = torch.empty(N * T, H, device=dev, dtype=x2d.dtype)
+        meta_idx = torch.empty(N * T, k, device=dev, dtype=torch.int32)
+        meta_w = torch.empty(N * T, k, device=dev, dtype=torch.float32)
+        ret_pos = torch.empty(T, N, device=dev, dtype=torch.int32)
+        with torch.cuda.device(dev):
+            K._lib.call("q35_ep_scatter", x2d.data_ptr(), idx.data_ptr(), weights.data_ptr(), T, k,
+                        H, El, N, send.data_ptr(), meta_idx.data_ptr(), meta_w.data_ptr(),
+                        ret_pos.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+        r_rows = ex.exchange(send)
+        r_idx = ex.exchange(meta_idx)
+        r_w = ex.exchange(meta_w)
+        mark("ep_dispatch")
+        # ---- receiver: local experts over the received slot lists
+        R = r_rows.shape[0]
+        lperm = K.moe_permute(r_idx, El)
+        # only offsets[El] of the R*k slots hold an expert: gather that many
+        xs = K.gather_rows(r_rows, lperm.sorted_tok, n_dev=lperm.offsets[El:])
+        act = K.grouped_gateup_swiglu(xs, self.gate_up_proj, lperm)
+        mark("gate_up_swiglu")
+        y = K.grouped_down(act, self.down_proj, lperm)
+        mark("down")
+        partial = K.moe_combine(y, r_w, lperm.slot_pos, None, R, H)
+        # ---- return: partial sums back to the senders, summed with the residual
+        back = ex.exchange(partial)
+        mark("ep_return")
+        ones = torch.ones(T, N, device=dev, dtype=torch.float32)
+        return K.moe_combine(back, ones, ret_pos, residual, T, H)

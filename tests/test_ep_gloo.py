@@ -1,6 +1,6 @@
-"""Expert-parallel exchange on CPU ranks (gloo): dispatch routes every row to
-the rank owning its expert in expert-major order, and combine returns the
-expert outputs to the sender in its original sorted order.  Also checks that
+"""Expert-parallel exchange on CPU ranks (gloo): each (token, rank) row with
+its slot list, in the fixed per-rank slab layout, reaches the rank that owns
+those experts, and the partial sums come back to the sender.  Also checks that
 a rank that dies before a collective surfaces as an error on the others (a
 short process-group timeout), not a hang."""
 import os
@@ -14,7 +14,6 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from oracle import layer_oracle as O
 
 
 def _port() -> int:
@@ -34,37 +33,46 @@ def _exchange_worker(rank, world, port, E, T, k, H, q):
     try:
         _init(rank, world, port)
         from qwen3_5_vl_cuda_custom_b200.ep import ExpertParallelExchange
+        ex = ExpertParallelExchange(E)
+        El = ex.E_local
         rng = np.random.default_rng(100 + rank)
         idx = np.stack([rng.choice(E, k, replace=False) for _ in range(T)])
         if rank == 0 and T > 3:
             idx[:3] = np.arange(k)  # several tokens on the same experts
-        counts, offsets, sorted_tok, slot_pos, _ = O.permutation(idx, E)
-        x = torch.randn(T, H, generator=torch.Generator().manual_seed(rank))
-        rows = x[torch.from_numpy(sorted_tok).long()]
-        ex = ExpertParallelExchange(E)
-        em, st = ex.dispatch(rows, torch.from_numpy(counts))
-        lo, hi = ex.expert_range
-        # expert-major layout: local expert e's rows are contiguous
-        offs = st.local_offsets.tolist()
-        assert offs[-1] == em.shape[0]
-        y = em.clone()
-        for e in range(hi - lo):
-            y[offs[e]:offs[e + 1]] *= float(lo + e + 1)  # "expert e" = scale by e + 1
-        back = ex.combine(y, st)
-        expert_of_row = np.repeat(np.arange(E), counts)
-        expect = rows * torch.from_numpy(expert_of_row + 1.0).float()[:, None]
-        assert torch.allclose(back, expect), "combine did not return the sender's rows"
-        # the combine over slot positions equals the per-token weighted sum
         w = torch.rand(T, k)
+        x = torch.randn(T, H, generator=torch.Generator().manual_seed(rank))
+        # sender slabs (the q35_ep_scatter layout): row d*T + t, slot lists local to d
+        dest = idx // El
+        send = torch.zeros(world * T, H)
+        meta_idx = torch.full((world * T, k), -1, dtype=torch.int32)
+        meta_w = torch.zeros(world * T, k)
+        ret_pos = torch.full((T, world), -1, dtype=torch.long)
+        for t in range(T):
+            for j in range(k):
+                d = int(dest[t, j])
+                send[d * T + t] = x[t]
+                meta_idx[d * T + t, j] = int(idx[t, j]) - d * El
+                meta_w[d * T + t, j] = w[t, j]
+                ret_pos[t, d] = d * T + t
+        r_rows, r_idx, r_w = ex.exchange(send), ex.exchange(meta_idx), ex.exchange(meta_w)
+        # receiver: "expert e" scales a row by (global e + 1); weighted per slot
+        lo, _ = ex.expert_range
+        partial = torch.zeros_like(r_rows)
+        for u in range(r_rows.shape[0]):
+            for j in range(k):
+                if int(r_idx[u, j]) >= 0:
+                    partial[u] += r_w[u, j] * r_rows[u] * float(lo + int(r_idx[u, j]) + 1)
+        back = ex.exchange(partial)
         out = torch.zeros(T, H)
-        sp = torch.from_numpy(slot_pos).long().view(T, k)
-        for j in range(k):
-            out += w[:, j:j + 1] * back[sp[:, j]]
+        for t in range(T):
+            for d in range(world):
+                if ret_pos[t, d] >= 0:
+                    out[t] += back[ret_pos[t, d]]
         ref = torch.zeros(T, H)
         for t in range(T):
             for j in range(k):
                 ref[t] += w[t, j] * x[t] * float(idx[t, j] + 1)
-        assert torch.allclose(out, ref, atol=1e-5)
+        assert torch.allclose(out, ref, atol=1e-5), "returned partial sums are wrong"
         dist.destroy_process_group()
         q.put((rank, "ok"))
     except Exception:  # pragma: no cover - reported to the parent
@@ -93,9 +101,8 @@ def _dying_worker(rank, world, port, q):
         ex = ExpertParallelExchange(8)
         if rank == 1:
             os._exit(3)  # leaves between steps, before the exchange
-        rows = torch.randn(4, 8)
         try:
-            ex.dispatch(rows, torch.tensor([1, 1, 1, 1, 0, 0, 0, 0]))
+            ex.exchange(torch.zeros(4, 8))
             q.put((rank, "no error"))
         except Exception as e:  # the surviving rank must see an error, not hang
             q.put((rank, f"error: {type(e).__name__}"))

@@ -1,7 +1,9 @@
 """Expert parallelism on 2+ GPUs (NCCL): each rank's output of an
-expert-parallel decoder layer equals, bit for bit, the single-GPU layer on the
-same input -- every expert row is computed by the same kernels with the same
-accumulation order wherever it runs.  Skipped with fewer than 2 GPUs."""
+expert-parallel decoder layer matches the single-GPU layer on the same input
+within the parity tolerance (the expert rows are computed by the same kernels;
+only the summation order of a token's experts and one bf16 rounding of each
+rank's partial sum differ), and the router logits are identical.  Skipped
+with fewer than 2 GPUs."""
 import os
 import socket
 import traceback
@@ -58,7 +60,10 @@ def _worker(rank, world, port, q):
                 y, rl, _ = ep_layer(x, rot.bind(pos))
                 yr, rlr, _ = ref_layer(x, rot.bind(pos))
             torch.cuda.synchronize()
-            results.append(bool(torch.equal(y, yr)) and bool(torch.equal(rl, rlr)))
+            from oracle import layer_oracle as O
+            st = O.error_stats(y.float().cpu(), yr.float().cpu())
+            results.append(bool(torch.equal(rl, rlr)) and st["max_abs_over_bf16"] <= 2e-2
+                           and st["mean_rel"] <= 5e-3)
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok" if all(results) else f"mismatch {results}"))

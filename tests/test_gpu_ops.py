@@ -176,6 +176,19 @@ def test_permutation_all_tokens_one_expert_set_and_empty_experts():
     _perm_case(idx, E)
 
 
+def test_permutation_negative_ids_are_empty_slots():
+    idx = np.array([[3, -1], [-1, 0], [3, 1], [-1, -1]])
+    got = K().moe_permute(torch.from_numpy(idx.astype(np.int32)).to(DEV), 4)
+    keep = [(t, j) for t in range(4) for j in range(2) if idx[t, j] >= 0]
+    assert got.counts.cpu().tolist() == [1, 1, 0, 2]
+    assert got.offsets.cpu().tolist() == [0, 1, 2, 2, 4]
+    assert got.sorted_tok.cpu()[:4].tolist() == [1, 2, 0, 2]
+    sp = got.slot_pos.cpu().view(4, 2)
+    assert all(sp[t, j] == -1 for t in range(4) for j in range(2) if idx[t, j] < 0)
+    assert len(keep) == 4
+    K().device_error_check()  # negative ids are not errors
+
+
 def test_permutation_skewed_zipf():
     rng = np.random.default_rng(1)
     T, E, k = 2048, 128, 8
