@@ -40,6 +40,11 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+# DRAM bytes (read + write) per launch from `ncu --set full` captures of the C2
+# workload (profiles/grouped_gemm_pair_c2_full.md, profiles/attention_tc2_c2_full.md)
+TRAFFIC_BYTES_C2 = {"gate_up_swiglu": 990.0e6, "down": 596.8e6, "attention": 42.7e6}
+# algorithmic bytes of the same launches (weights + rows read, outputs written)
+ALGO_BYTES_C2 = {"gate_up_swiglu": 989.8e6, "down": 587.2e6, "attention": 75.5e6}
 LINK_GBS = 770.0  # measured NVLink peer copy per direction on this pool
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -480,7 +485,11 @@ def run_ours(args, world, rank, local):
                   "note": "same layer through the module API without graph replay"},
         "gpu_launches": LAUNCHES_PER_LAYER * args.steps,
         "roofline": {"bound": bound, "kernel": top, "achieved": achieved, "peak": peak, "unit": unit,
-                     "frac": achieved / peak, "traffic": None, "peak_source": peak_src},
+                     "frac": achieved / peak,
+                     "traffic": TRAFFIC_BYTES_C2.get(top) if S == 4096 else None,
+                     "algorithmic": amount,
+                     "algorithmic_bytes": ALGO_BYTES_C2.get(top) if S == 4096 else None,
+                     "peak_source": peak_src},
         "breakdown": breakdown,
         "cpu_baseline": cpu,
         "clocks": clocks,
