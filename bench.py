@@ -143,6 +143,7 @@ def stage_table(cfg, T: int, S: int, world: int = 1) -> dict:
         "input_rmsnorm": ("hbm", 2 * T * H * 2),
         "qkv_gemm": ("tensor", 2 * T * H * (Hq + 2 * Hkv) * D),
         "qknorm_mrope": ("hbm", T * (Hq + 2 * Hkv) * D * 2 * 2),
+        "qkv_norm_rope": ("tensor", 2 * T * H * (Hq + 2 * Hkv) * D),
         "attention": ("tensor", B * Hq * 4 * D * S * (S + 1) / 2),
         "o_proj_residual": ("tensor", 2 * T * Hq * D * H),
         "post_rmsnorm": ("hbm", 2 * T * H * 2),
@@ -155,6 +156,7 @@ def stage_table(cfg, T: int, S: int, world: int = 1) -> dict:
         # expert parallelism: one row per (token, destination rank), each
         # direction; expected ranks per token N(1 - (1 - 1/N)^k), N = world
         "ep_dispatch": ("link", T * H * 2 * world * (1 - (1 - 1 / world) ** k)),
+        "experts_chunk0": ("tensor", T * k * 2 * 3 * H * I / 2),
         "ep_return": ("link", T * H * 2 * world * (1 - (1 - 1 / world) ** k)),
     }
 
@@ -176,12 +178,18 @@ def staged_forward(layer, rot, x, pos, marks=None):
     xn = K.rmsnorm(x, layer.input_layernorm.weight, layer.input_layernorm.eps)
     mark("input_rmsnorm")
     w, _ = att._qkv_weight()
-    qkv = K.matmul(xn, w)
-    mark("qkv_gemm")
-    q, k, v = K.qknorm_mrope(qkv, att.q_norm.weight, att.k_norm.weight, pos, rot.inv_freq,
-                             rot.mrope_section, B, S, att.num_heads, att.num_kv_heads, att.head_dim,
-                             att.q_norm.eps)
-    mark("qknorm_mrope")
+    if att.fuse_qkv_epilogue and att.head_dim == 128 and B * S >= 256:
+        q, k, v = K.qkv_proj_norm_rope(xn, w, att.q_norm.weight, att.k_norm.weight, pos,
+                                       rot.inv_freq, rot.mrope_section, att.num_heads,
+                                       att.num_kv_heads, att.q_norm.eps)
+        mark("qkv_norm_rope")
+    else:
+        qkv = K.matmul(xn, w)
+        mark("qkv_gemm")
+        q, k, v = K.qknorm_mrope(qkv, att.q_norm.weight, att.k_norm.weight, pos, rot.inv_freq,
+                                 rot.mrope_section, B, S, att.num_heads, att.num_kv_heads,
+                                 att.head_dim, att.q_norm.eps)
+        mark("qknorm_mrope")
     o = K.attention_tokens(q, k, v, att.scale, True)
     mark("attention")
     h = K.matmul(o, att.o_proj.weight, residual=x, out_dtype=torch.float32)
@@ -191,12 +199,12 @@ def staged_forward(layer, rot, x, pos, marks=None):
     m2 = m_in.reshape(-1, H)
     logits, idx, wts = moe.route(m2)
     mark("router")
-    perm = K.moe_permute(idx, moe.num_experts)
-    mark("permute")
     if getattr(moe, "exchange", None) is not None:  # expert parallel
         out = moe.experts(m2, idx, wts, h.reshape(-1, H), mark=mark)
         mark("combine_residual")
         return out.reshape(B, S, H)
+    perm = K.moe_permute(idx, moe.num_experts)
+    mark("permute")
     xs = K.gather_rows(m2, perm.sorted_tok)
     mark("gather")
     gu_p, dn_p = moe._packed_experts()
@@ -209,7 +217,7 @@ def staged_forward(layer, rot, x, pos, marks=None):
     return out.reshape(B, S, H)
 
 
-LAUNCHES_PER_LAYER = 15  # rmsnorm, qkv, qknorm, attn, o, rmsnorm, router, permute x3, gather, gu, down, combine
+LAUNCHES_PER_LAYER = 15  # rmsnorm, rope table, qkv+norm+rope, attn, o, rmsnorm, router, permute x3, gather, gu, down, combine
 
 
 def cpu_reference_step_fn(cfg, P, x_cpu, pos_cpu, dtype):

@@ -58,6 +58,11 @@ Q35_API const char *q35_last_error_message(void);
 Q35_API int q35_device_error_check(int32_t *info4);
 /* Library build identity, e.g. "q35b200 sm_100a". */
 Q35_API const char *q35_version(void);
+/* Caps the grid of the persistent kernels (GEMMs) launched from this host
+ * thread at n SMs (0: all SMs), so that work running at the same time -- e.g.
+ * the collective kernels of an overlapped expert-parallel exchange -- keeps
+ * some SMs.  No reference counterpart.                                     */
+Q35_API int q35_set_sm_limit(int n);
 
 /* ---- RMSNorm ------------------------------------------------------------
  * y[r,:] = bf16( x[r,:] * rsqrt(mean(x[r,:]^2) + eps) * w ), fp32 inside.
@@ -94,6 +99,22 @@ Q35_API int q35_qknorm_mrope_fwd(const void *qkv, const void *qw, const void *kw
                          const int32_t *sections, int interleaved, void *q,
                          void *k, void *v, int64_t B, int64_t S, int Hq,
                          int Hkv, int D, float eps, q35_stream_t stream);
+
+/* The q/k/v projection with QK-norm + mRoPE fused into its epilogue (head_dim
+ * 128): x bf16 [B*S, H] times w_qkv bf16 [(Hq + 2 Hkv) * 128, H] (q, k, v
+ * projection weights stacked), then per head RMSNorm (q_w / k_w, bf16 [128])
+ * and rotate-half mRoPE for q and k, written head-major q [B,Hq,S,128],
+ * k, v [B,Hkv,S,128] -- the same results as q35_gemm_bf16 followed by
+ * q35_qknorm_mrope_fwd without the [B*S, (Hq+2Hkv)*128] intermediate.
+ * workspace: fp32 [2 * B * S * 64] (rotary table).  Hq + 2 Hkv even.
+ * Replaces q/k/v CudaLinear + q_norm/k_norm + TextMRoPE.apply
+ * (REF modules/attention.py:82-87).                                        */
+Q35_API int q35_qkv_proj_norm_rope(const void *x, const void *w_qkv, const void *q_w,
+                                   const void *k_w, const int64_t *positions,
+                                   const float *inv_freq, const int32_t *sections,
+                                   int interleaved, void *q, void *k, void *v, int64_t B,
+                                   int64_t S, int H, int Hq, int Hkv, float eps,
+                                   float *workspace, q35_stream_t stream);
 
 /* Apply mRoPE to a head-major tensor x [B,H,S,D] in place of
  * mrope_forward(x, cos, sin) (REF csrc/mrope_op.cpp:5-7), computing cos/sin
@@ -193,12 +214,14 @@ Q35_API int q35_moe_permute_noalloc(const int32_t *idx, int64_t T, int k, int E,
  * (idx int32 [T, k], global ids) is owned by rank d (experts
  * [d*El, (d+1)*El)), else left untouched.  meta_idx int32 [N, T, k] holds, at
  * slot j, the slot's expert id local to rank d or -1, meta_w fp32 [N, T, k]
- * its weight (w fp32 [T, k]) or 0; ret_pos int32 [T, N] = d*T + t for the
+ * its weight (w fp32 [T, k]) or 0 (slab d of each starts meta_slab >= T*k
+ * elements after slab d-1, so both can interleave in one buffer); ret_pos int32 [T, N] = d*T + t for the
  * ranks token t uses, else -1.  k <= 16, N <= 32.  An even-split all-to-all
  * of these slabs needs no host-side sizes.  No reference counterpart.       */
 Q35_API int q35_ep_scatter(const void *x, const int32_t *idx, const float *w, int64_t T, int k,
                            int64_t H, int El, int N, void *send, int32_t *meta_idx,
-                           float *meta_w, int32_t *ret_pos, q35_stream_t stream);
+                           float *meta_w, int64_t meta_slab, int32_t *ret_pos,
+                           q35_stream_t stream);
 
 /* dst[r,:] = src[rows[r],:] for r < n (bf16, cols % 8 == 0); n may be read
  * from device memory (n_dev != NULL: *n_dev rows, at most n_max).           */

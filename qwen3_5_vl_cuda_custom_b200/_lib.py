@@ -21,10 +21,14 @@ _SIGS = {
     "q35_last_error_message": (c_char_p, []),
     "q35_device_error_check": (c_int, [_i32p]),
     "q35_version": (c_char_p, []),
+    "q35_set_sm_limit": (c_int, [c_int]),
     "q35_rmsnorm_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
     "q35_qknorm_mrope_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, _i32p, c_int,
                                      c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int,
                                      c_int, c_float, c_void_p]),
+    "q35_qkv_proj_norm_rope": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, _i32p,
+                                       c_int, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int,
+                                       c_int, c_int, c_float, c_void_p, c_void_p]),
     "q35_mrope_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, _i32p, c_int, c_int64, c_int,
                               c_int64, c_int, c_void_p]),
     "q35_router_topk_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
@@ -43,7 +47,7 @@ _SIGS = {
     "q35_moe_permute_noalloc": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_void_p, c_void_p]),
     "q35_ep_scatter": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_int, c_int,
-                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+                               c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
     "q35_gather_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p]),
     "q35_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                               c_int64, c_void_p]),

@@ -54,6 +54,8 @@ int *device_error_word() {
   return g_err_word[dev];
 }
 
+thread_local int g_sm_limit = 0;  // 0: all SMs
+
 int num_sms() {
   int dev = 0;
   if (current_device(&dev) != Q35_OK) return 1;
@@ -62,7 +64,8 @@ int num_sms() {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     g_num_sms[dev] = n > 0 ? n : 1;
   }
-  return g_num_sms[dev];
+  const int hw = g_num_sms[dev];
+  return (g_sm_limit > 0 && g_sm_limit < hw) ? g_sm_limit : hw;
 }
 
 int ensure_smem_attr(const void *kernel, int bytes) {
@@ -138,6 +141,12 @@ const char *q35_status_string(int status) {
 const char *q35_last_error_message(void) { return q35::g_last_msg; }
 
 const char *q35_version(void) { return "q35b200 sm_100a"; }
+
+int q35_set_sm_limit(int n) {
+  if (n < 0) return q35::fail(Q35_ERR_INVALID, "sm limit %d < 0", n);
+  q35::g_sm_limit = n;
+  return Q35_OK;
+}
 
 int q35_device_error_check(int32_t *info4) {
   int *w = q35::device_error_word();

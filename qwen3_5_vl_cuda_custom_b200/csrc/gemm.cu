@@ -38,7 +38,7 @@ constexpr int kBK = 64;  // 64 bf16 = one 128-byte swizzle row
 constexpr int kThreads = 192;
 constexpr int kMaxGroups = 512;
 
-enum Epilogue { EPI_PLAIN = 0, EPI_SWIGLU = 1 };
+enum Epilogue { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_QKV = 2 };
 
 struct GemmParams {
   int M;                       // dense rows (grouped: unused)
@@ -62,6 +62,14 @@ struct GemmParams {
   int k_splits;                // dense only: K split into this many partial planes
   int64_t split_stride;        // elements between partial output planes
   int b_packed;                // B stored as contiguous 128 x 64 tiles (see q35_pack_b_tiles)
+  // EPI_QKV: the output columns are Hq + 2*Hkv heads of 128; q/k heads get
+  // RMSNorm (qk_w: q weight [128] then k weight [128]) and rotate-half RoPE
+  // (cos/sin tables fp32 [rows, 64]); q, k, v are written head-major.
+  const uint16_t *q_norm_w, *k_norm_w;
+  const float *rope_cos, *rope_sin;
+  uint16_t *q_out, *k_out, *v_out;
+  int Hq, Hkv, seq;
+  float eps;
 };
 
 template <int BN, int STAGES>
@@ -143,6 +151,29 @@ __device__ __forceinline__ void store32(uint16_t *dst, const float *v) {
 __device__ __forceinline__ void load32(const uint16_t *src, float *v) {
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
+    const uint4 u = reinterpret_cast<const uint4 *>(src)[q];
+    unpack_bf2(u.x, v[8 * q + 0], v[8 * q + 1]);
+    unpack_bf2(u.y, v[8 * q + 2], v[8 * q + 3]);
+    unpack_bf2(u.z, v[8 * q + 4], v[8 * q + 5]);
+    unpack_bf2(u.w, v[8 * q + 6], v[8 * q + 7]);
+  }
+}
+
+__device__ __forceinline__ void store16(uint16_t *dst, const float *v) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    uint4 u;
+    u.x = pack_bf2(v[8 * q + 0], v[8 * q + 1]);
+    u.y = pack_bf2(v[8 * q + 2], v[8 * q + 3]);
+    u.z = pack_bf2(v[8 * q + 4], v[8 * q + 5]);
+    u.w = pack_bf2(v[8 * q + 6], v[8 * q + 7]);
+    reinterpret_cast<uint4 *>(dst)[q] = u;
+  }
+}
+
+__device__ __forceinline__ void load16(const uint16_t *src, float *v) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
     const uint4 u = reinterpret_cast<const uint4 *>(src)[q];
     unpack_bf2(u.x, v[8 * q + 0], v[8 * q + 1]);
     unpack_bf2(u.y, v[8 * q + 2], v[8 * q + 3]);
@@ -603,6 +634,91 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+      } else if constexpr (EPI == EPI_QKV) {
+        // Two 128-wide heads per 256-column tile; this thread owns one token.
+        // Pass 1: inverse RMS of each q/k head.  Pass 2: 16-column blocks of
+        // the rotate-half pairs (c, c + 64); the block's cos/sin (float4
+        // loads) serve both heads.
+        const int head0 = ti.nt * 2;
+        const int n_qk = max(0, min(2, p.Hq + p.Hkv - head0));  // q/k heads in this tile
+        float rinv[2] = {1.f, 1.f};
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          if (hh < n_qk) {
+            float ss = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t x[32];
+              sm100::tmem_ld32(t_row + hh * 128 + c * 32, x);
+              sm100::tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) ss = fmaf(__uint_as_float(x[i]), __uint_as_float(x[i]), ss);
+            }
+            rinv[hh] = rsqrtf(ss * (1.f / 128.f) + p.eps);
+          }
+        }
+        const int64_t b = row / p.seq, sq = row - b * p.seq;
+        uint16_t *dst[2];
+        const uint16_t *wn[2];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int head = head0 + hh;
+          if (head < p.Hq) {
+            dst[hh] = p.q_out + ((b * p.Hq + head) * p.seq + sq) * 128;
+            wn[hh] = p.q_norm_w;
+          } else if (head < p.Hq + p.Hkv) {
+            dst[hh] = p.k_out + ((b * p.Hkv + (head - p.Hq)) * p.seq + sq) * 128;
+            wn[hh] = p.k_norm_w;
+          } else {
+            dst[hh] = p.v_out + ((b * p.Hkv + (head - p.Hq - p.Hkv)) * p.seq + sq) * 128;
+            wn[hh] = nullptr;
+          }
+        }
+        const float4 *cs4 = reinterpret_cast<const float4 *>(p.rope_cos + (valid ? row : 0) * 64);
+        const float4 *sn4 = reinterpret_cast<const float4 *>(p.rope_sin + (valid ? row : 0) * 64);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float cc[16], sn[16];
+          if (valid && n_qk > 0) {
+#pragma unroll
+            for (int v4 = 0; v4 < 4; ++v4) {
+              const float4 a = cs4[c * 4 + v4], s4 = sn4[c * 4 + v4];
+              cc[4 * v4] = a.x; cc[4 * v4 + 1] = a.y; cc[4 * v4 + 2] = a.z; cc[4 * v4 + 3] = a.w;
+              sn[4 * v4] = s4.x; sn[4 * v4 + 1] = s4.y; sn[4 * v4 + 2] = s4.z; sn[4 * v4 + 3] = s4.w;
+            }
+          }
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            uint32_t x1[16], x2[16];
+            sm100::tmem_ld16(t_row + hh * 128 + c * 16, x1);
+            sm100::tmem_ld16(t_row + hh * 128 + 64 + c * 16, x2);
+            sm100::tmem_wait_ld();
+            if (valid) {  // no early exit: every tcgen05.ld needs the whole warp
+              float o1[16], o2[16];
+              if (hh >= n_qk) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  o1[i] = __uint_as_float(x1[i]);
+                  o2[i] = __uint_as_float(x2[i]);
+                }
+              } else {
+                float w1[16], w2[16];
+                load16(wn[hh] + c * 16, w1);
+                load16(wn[hh] + 64 + c * 16, w2);
+                const float r = rinv[hh];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const float y1 = (__uint_as_float(x1[i]) * r) * w1[i];
+                  const float y2 = (__uint_as_float(x2[i]) * r) * w2[i];
+                  o1[i] = y1 * cc[i] - y2 * sn[i];
+                  o2[i] = y2 * cc[i] + y1 * sn[i];
+                }
+              }
+              store16(dst[hh] + c * 16, o1);
+              store16(dst[hh] + 64 + c * 16, o2);
+            }
+          }
+        }
       } else {
         const int n0 = ti.nt * (BN / 2);
 #pragma unroll 1
@@ -672,6 +788,29 @@ __global__ void pack_b_tiles_kernel(const uint16_t *__restrict__ src,
   const int64_t rb = r / 128, rin = r % 128;
   const int64_t d = ((rb * kb_n + kb) * 128 + rin) * 64 + cin;
   *reinterpret_cast<uint4 *>(dst + d) = *reinterpret_cast<const uint4 *>(src + r * K + c8 * 8);
+}
+
+
+// cos/sin [rows, 64] of the rotary angles pos[axis(j)] * inv_freq[j] (fp32,
+// precise sincosf), with axis(j) from the mRoPE section layout: chunked
+// (interleaved == 0, REF cuda_qwen3_vl/kernels/mrope.py:19-35) or HF's T/H/W
+// interleave.  One thread per (row, j).
+__global__ void rope_table_kernel(const int64_t *__restrict__ pos, const float *__restrict__ inv_freq,
+                                  int s0, int s1, int s2, int interleaved, int64_t rows,
+                                  float *__restrict__ cos_t, float *__restrict__ sin_t) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * 64) return;
+  const int64_t row = i / 64;
+  const int j = static_cast<int>(i % 64);
+  int ax;
+  if (interleaved)
+    ax = ((j % 3) == 1 && j < 3 * s1) ? 1 : (((j % 3) == 2 && j < 3 * s2) ? 2 : 0);
+  else
+    ax = j < s0 ? 0 : (j < s0 + s1 ? 1 : 2);
+  float sn, cs;
+  sincosf(static_cast<float>(pos[ax * rows + row]) * inv_freq[j], &sn, &cs);
+  cos_t[i] = cs;
+  sin_t[i] = sn;
 }
 
 }  // namespace
@@ -817,6 +956,66 @@ extern "C" int q35_pack_b_tiles(const void *src, void *dst, int64_t rows, int64_
       static_cast<const uint16_t *>(src), static_cast<uint16_t *>(dst), rows, K);
   Q35_LAUNCH_CHECK("pack_b_tiles launch");
   return Q35_OK;
+}
+
+// Fused q/k/v projection: GEMM of x [B*S, H] with the concatenated weight
+// w_qkv [(Hq + 2 Hkv) * 128, H] on CTA pairs, whose epilogue applies the
+// per-head RMSNorm (q_norm / k_norm weights) and the mRoPE rotation to the q
+// and k heads and writes q [B,Hq,S,128], k and v [B,Hkv,S,128] head-major.
+// workspace: fp32 [2 * B * S * 64] for the rotary cos/sin table.
+extern "C" int q35_qkv_proj_norm_rope(const void *x, const void *w_qkv, const void *q_w,
+                                      const void *k_w, const int64_t *positions,
+                                      const float *inv_freq, const int32_t *sections,
+                                      int interleaved, void *q, void *k, void *v, int64_t B,
+                                      int64_t S, int H, int Hq, int Hkv, float eps,
+                                      float *workspace, q35_stream_t stream) {
+  if (!x || !w_qkv || !q_w || !k_w || !positions || !inv_freq || !sections || !q || !k || !v ||
+      !workspace)
+    return fail(Q35_ERR_INVALID, "qkv_proj_norm_rope: null pointer");
+  const int64_t M = B * S;
+  const int heads = Hq + 2 * Hkv;
+  if (M <= 0 || H <= 0 || H % 8 != 0 || Hq <= 0 || Hkv <= 0 || heads % 2 != 0)
+    return fail(Q35_ERR_SHAPE, "qkv_proj_norm_rope: H %d (x8), heads %d (even)", H, heads);
+  if (sections[0] + sections[1] + sections[2] != 64)
+    return fail(Q35_ERR_SHAPE, "qkv_proj_norm_rope: sections must sum to 64 (head_dim 128)");
+  if (M >= (int64_t(1) << 31)) return fail(Q35_ERR_SHAPE, "qkv_proj_norm_rope: too many rows");
+  int *err = device_error_word();
+  if (!err) return fail(Q35_ERR_CUDA, "qkv_proj_norm_rope: no device error word");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  float *cos_t = workspace, *sin_t = workspace + M * 64;
+  rope_table_kernel<<<static_cast<unsigned>((M * 64 + 255) / 256), 256, 0, s>>>(
+      positions, inv_freq, sections[0], sections[1], sections[2], interleaved ? 1 : 0, M, cos_t,
+      sin_t);
+  Q35_LAUNCH_CHECK("rope_table launch");
+  const int64_t N = static_cast<int64_t>(heads) * 128;
+  CUtensorMap ta, tb;
+  int st = make_tmap_bf16_2d(&ta, x, H, M, static_cast<uint64_t>(H) * 2, kBK, kBM);
+  if (st) return st;
+  st = make_tmap_bf16_2d(&tb, w_qkv, H, N, static_cast<uint64_t>(H) * 2, kBK, 128);
+  if (st) return st;
+  GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.E = 1;
+  p.N = static_cast<int>(N);
+  p.K = H;
+  p.n_tiles = heads / 2;
+  p.b_rows_per_group = static_cast<int>(N);
+  p.b_tile_step = 256;
+  p.b_second_off = 128;
+  p.err = err;
+  p.q_norm_w = static_cast<const uint16_t *>(q_w);
+  p.k_norm_w = static_cast<const uint16_t *>(k_w);
+  p.rope_cos = cos_t;
+  p.rope_sin = sin_t;
+  p.q_out = static_cast<uint16_t *>(q);
+  p.k_out = static_cast<uint16_t *>(k);
+  p.v_out = static_cast<uint16_t *>(v);
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.seq = static_cast<int>(S);
+  p.eps = eps;
+  const int pair_tiles = static_cast<int>(((M + 255) / 256) * p.n_tiles);
+  return launch_gemm_pair<EPI_QKV>(ta, tb, p, pair_tiles, s);
 }
 
 static int grouped_common(const void *a, const void *w, void *out,

@@ -478,7 +478,8 @@ namespace {
 __global__ void __launch_bounds__(256) ep_scatter_kernel(
     const uint16_t *__restrict__ x, const int32_t *__restrict__ idx, const float *__restrict__ w,
     int64_t T, int k, int64_t H, int El, int N, uint16_t *__restrict__ send,
-    int32_t *__restrict__ meta_idx, float *__restrict__ meta_w, int32_t *__restrict__ ret_pos) {
+    int32_t *__restrict__ meta_idx, float *__restrict__ meta_w, int64_t meta_slab,
+    int32_t *__restrict__ ret_pos) {
   const int64_t t = blockIdx.x;
   __shared__ int s_e[16];
   __shared__ uint32_t s_used;  // bit d: token t sends to rank d (N <= 32)
@@ -495,10 +496,10 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(
   for (int i = threadIdx.x; i < N * k; i += blockDim.x) {
     const int d = i / k, j = i % k;
     const int e = s_e[j];
-    const int64_t row = static_cast<int64_t>(d) * T + t;
+    const int64_t m = static_cast<int64_t>(d) * meta_slab + t * k + j;
     const bool mine = e >= 0 && e / El == d;
-    meta_idx[row * k + j] = mine ? e - d * El : -1;
-    meta_w[row * k + j] = mine ? w[t * k + j] : 0.f;
+    meta_idx[m] = mine ? e - d * El : -1;
+    meta_w[m] = mine ? w[t * k + j] : 0.f;
   }
   for (int d = threadIdx.x; d < N; d += blockDim.x)
     ret_pos[t * N + d] = ((used >> d) & 1u) ? static_cast<int32_t>(d * T + t) : -1;
@@ -515,17 +516,19 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(
 
 extern "C" int q35_ep_scatter(const void *x, const int32_t *idx, const float *w, int64_t T,
                               int k, int64_t H, int El, int N, void *send, int32_t *meta_idx,
-                              float *meta_w, int32_t *ret_pos, q35_stream_t stream) {
+                              float *meta_w, int64_t meta_slab, int32_t *ret_pos,
+                              q35_stream_t stream) {
   if (!send || !meta_idx || !meta_w || !ret_pos || (T > 0 && (!x || !idx || !w)))
     return fail(Q35_ERR_INVALID, "ep_scatter: null pointer");
   if (T < 0 || k < 1 || k > 16 || El < 1 || N < 1 || N > 32 || H <= 0 || H % 8 != 0)
     return fail(Q35_ERR_SHAPE, "ep_scatter: k %d (<=16) N %d (<=32) H %lld (x8)", k, N,
                 (long long)H);
   if (!aligned16(x) || !aligned16(send)) return fail(Q35_ERR_ALIGN, "ep_scatter: alignment");
+  if (meta_slab < T * k) return fail(Q35_ERR_SHAPE, "ep_scatter: meta_slab < T*k");
   if (T == 0) return Q35_OK;
   ep_scatter_kernel<<<static_cast<unsigned>(T), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t *>(x), idx, w, T, k, H, El, N, static_cast<uint16_t *>(send),
-      meta_idx, meta_w, ret_pos);
+      meta_idx, meta_w, meta_slab, ret_pos);
   Q35_LAUNCH_CHECK("ep_scatter launch");
   return Q35_OK;
 }

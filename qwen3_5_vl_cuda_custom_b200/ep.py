@@ -85,40 +85,89 @@ class ExpertParallelSparseMoE(CudaSparseMoE):
                 state_dict[key] = t[lo:hi]
         super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
 
-    def experts(self, x2d: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor,
-                residual: torch.Tensor | None = None, mark=None) -> torch.Tensor:
-        """``mark(name)`` (optional) is called after each stage (benchmark timing)."""
-        mark = mark or (lambda name: None)
-        T, H = x2d.shape
+    ep_chunks = 2  # token chunks whose exchange overlaps the other chunk's experts
+    ep_sm_reserve = 32  # SMs left to the collectives while the expert GEMMs run
+
+    def _chunk_send(self, x2d, idx, w):
+        """Send slabs of one token chunk: rows [N*Tc, H] and slot lists packed as
+        [N, 2, Tc, k] int32 (expert ids, then the weights' bits)."""
+        Tc, H = x2d.shape
         k = idx.shape[1]
-        ex = self.exchange
-        N, El = ex.world, ex.E_local
+        N, El = self.exchange.world, self.exchange.E_local
         dev = x2d.device
-        # ---- sender: slab d holds the rows and slot lists for rank d
-        send = torch.empty(N * T, H, device=dev, dtype=x2d.dtype)
-        meta_idx = torch.empty(N * T, k, device=dev, dtype=torch.int32)
-        meta_w = torch.empty(N * T, k, device=dev, dtype=torch.float32)
-        ret_pos = torch.empty(T, N, device=dev, dtype=torch.int32)
+        send = torch.empty(N * Tc, H, device=dev, dtype=x2d.dtype)
+        meta = torch.empty(N, 2, Tc, k, device=dev, dtype=torch.int32)
+        ret_pos = torch.empty(Tc, N, device=dev, dtype=torch.int32)
         with torch.cuda.device(dev):
-            K._lib.call("q35_ep_scatter", x2d.data_ptr(), idx.data_ptr(), weights.data_ptr(), T, k,
-                        H, El, N, send.data_ptr(), meta_idx.data_ptr(), meta_w.data_ptr(),
+            K._lib.call("q35_ep_scatter", x2d.data_ptr(), idx.data_ptr(), w.data_ptr(), Tc, k, H, El, N,
+                        send.data_ptr(), meta.data_ptr(), meta[:, 1].data_ptr(), 2 * Tc * k,
                         ret_pos.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
-        r_rows = ex.exchange(send)
-        r_idx = ex.exchange(meta_idx)
-        r_w = ex.exchange(meta_w)
-        mark("ep_dispatch")
-        # ---- receiver: local experts over the received slot lists
-        R = r_rows.shape[0]
+        return send, meta, ret_pos
+
+    def _chunk_experts(self, r_rows, r_meta):
+        """Local experts over one chunk's received slot lists -> bf16 partial sums."""
+        N, El = self.exchange.world, self.exchange.E_local
+        R, H = r_rows.shape
+        r_idx = r_meta[:, 0].reshape(R, -1).contiguous()
+        r_w = r_meta[:, 1].reshape(R, -1).contiguous().view(torch.float32)
         lperm = K.moe_permute(r_idx, El)
         # only offsets[El] of the R*k slots hold an expert: gather that many
         xs = K.gather_rows(r_rows, lperm.sorted_tok, n_dev=lperm.offsets[El:])
         act = K.grouped_gateup_swiglu(xs, self.gate_up_proj, lperm)
-        mark("gate_up_swiglu")
         y = K.grouped_down(act, self.down_proj, lperm)
-        mark("down")
-        partial = K.moe_combine(y, r_w, lperm.slot_pos, None, R, H)
-        # ---- return: partial sums back to the senders, summed with the residual
-        back = ex.exchange(partial)
+        return K.moe_combine(y, r_w, lperm.slot_pos, None, R, H)
+
+    def _run_chunks(self, inflight, returns, grp, mark):
+        for c, (r_rows, r_meta, w1, w2) in enumerate(inflight):
+            w1.wait()
+            w2.wait()
+            if c == 0:
+                mark("ep_dispatch")
+            partial = self._chunk_experts(r_rows, r_meta)
+            if c == 0:
+                mark("experts_chunk0")
+            back = torch.empty_like(partial)
+            returns.append((back, dist.all_to_all_single(back, partial, group=grp, async_op=True)))
+
+    def experts(self, x2d: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor,
+                residual: torch.Tensor | None = None, mark=None) -> torch.Tensor:
+        """``mark(name)`` (optional) is called after each stage (benchmark timing).
+
+        Tokens are processed in ``ep_chunks`` chunks: all dispatches are issued
+        first (asynchronous all-to-alls on the communicator's stream), then each
+        chunk's experts run as soon as its rows arrive and its return is issued
+        right after, so chunk c+1's dispatch and chunk c's return overlap the
+        expert GEMMs of the other chunk."""
+        mark = mark or (lambda name: None)
+        T, H = x2d.shape
+        N = self.exchange.world
+        grp = self.exchange.group
+        # NCCL's copy kernels share SMs and HBM with the expert GEMMs: overlap
+        # only pays where the exchange is large relative to the experts (N >= 4)
+        chunks = self.ep_chunks if (T >= 256 * self.ep_chunks and N >= 4) else 1
+        bounds = [T * c // chunks for c in range(chunks + 1)]
+        sends = [self._chunk_send(x2d[a:b], idx[a:b].contiguous(), weights[a:b].contiguous())
+                 for a, b in zip(bounds[:-1], bounds[1:])]
+        inflight = []
+        for send, meta, _ in sends:
+            r_rows, r_meta = torch.empty_like(send), torch.empty_like(meta)
+            w1 = dist.all_to_all_single(r_rows, send, group=grp, async_op=True)
+            w2 = dist.all_to_all_single(r_meta, meta, group=grp, async_op=True)
+            inflight.append((r_rows, r_meta, w1, w2))
+        returns = []
+        n_sms = torch.cuda.get_device_properties(x2d.device).multi_processor_count
+        if chunks > 1 and self.ep_sm_reserve:
+            K._lib.call("q35_set_sm_limit", max(2, n_sms - self.ep_sm_reserve))
+        try:
+            self._run_chunks(inflight, returns, grp, mark)
+        finally:
+            K._lib.call("q35_set_sm_limit", 0)
+        out = torch.empty(T, H, device=x2d.device, dtype=torch.bfloat16)
+
+        ones = torch.ones(max(bounds[1] - bounds[0], 1), N, device=x2d.device, dtype=torch.float32)
+        for (a, b), (_, _, ret_pos), (back, work) in zip(zip(bounds[:-1], bounds[1:]), sends, returns):
+            work.wait()
+            res = None if residual is None else residual[a:b]
+            K.moe_combine(back, ones[: b - a], ret_pos, res, b - a, H, out=out[a:b])
         mark("ep_return")
-        ones = torch.ones(T, N, device=dev, dtype=torch.float32)
-        return K.moe_combine(back, ones, ret_pos, residual, T, H)
+        return out

@@ -278,7 +278,8 @@ def grouped_down(act: torch.Tensor, w_down: torch.Tensor, perm: Permutation,
 
 
 def moe_combine(y: torch.Tensor, weights: torch.Tensor, slot_pos: torch.Tensor,
-                residual: torch.Tensor | None, T: int, H: int) -> torch.Tensor:
+                residual: torch.Tensor | None, T: int, H: int,
+                out: torch.Tensor | None = None) -> torch.Tensor:
     """out[t] = residual[t] + sum_j weights[t,j] * y[slot_pos[t,j]] (fp32 sum, bf16 out)."""
     y = _require(y, "combine.y")
     weights = _require(weights, "combine.weights", torch.float32)
@@ -287,7 +288,10 @@ def moe_combine(y: torch.Tensor, weights: torch.Tensor, slot_pos: torch.Tensor,
     if residual is not None:
         residual = _require(residual, "combine.residual", (_BF16, torch.float32))
     r32 = 1 if residual is not None and residual.dtype == torch.float32 else 0
-    out = torch.empty(T, H, device=weights.device, dtype=_BF16)
+    if out is None:
+        out = torch.empty(T, H, device=weights.device, dtype=_BF16)
+    elif out.dtype != _BF16 or not out.is_contiguous() or out.numel() != T * H:
+        raise RuntimeError("moe_combine: out must be a contiguous bf16 [T, H] tensor")
     with torch.cuda.device(weights.device):
         _lib.call("q35_moe_combine", y.data_ptr(), weights.data_ptr(), slot_pos.data_ptr(),
                   _ptr(residual), r32, out.data_ptr(), T, k, H, _stream(weights))
@@ -313,6 +317,35 @@ def qknorm_mrope(qkv: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor,
                   pos.data_ptr(), inv.data_ptr(), _lib.sections_arg(mrope_section),
                   1 if interleaved else 0, q.data_ptr(), k.data_ptr(), v.data_ptr(), B, S, Hq, Hkv,
                   D, float(eps), _stream(qkv))
+    return q, k, v
+
+
+def qkv_proj_norm_rope(x: torch.Tensor, w_qkv: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor,
+                       position_ids: torch.Tensor, inv_freq: torch.Tensor, mrope_section,
+                       Hq: int, Hkv: int, eps: float, interleaved: bool = False):
+    """q/k/v projection of x (B,S,H) with QK-RMSNorm + mRoPE + head-major split
+    in the GEMM epilogue (head_dim 128, no projection bias): the result of
+    matmul(x, w_qkv) followed by qknorm_mrope, with the projection kept in fp32
+    until the rotated head is written."""
+    x = _require(x, "qkv_proj_norm_rope.x")
+    w_qkv = _require(w_qkv, "qkv_proj_norm_rope.w_qkv")
+    q_w = _require(q_w, "qkv_proj_norm_rope.q_w")
+    k_w = _require(k_w, "qkv_proj_norm_rope.k_w")
+    pos = _require(position_ids.to(torch.int64), "qkv_proj_norm_rope.position_ids", torch.int64)
+    inv = _require(inv_freq, "qkv_proj_norm_rope.inv_freq", torch.float32)
+    B, S, H = x.shape
+    if w_qkv.shape != ((Hq + 2 * Hkv) * 128, H):
+        raise RuntimeError(f"qkv_proj_norm_rope: w_qkv {tuple(w_qkv.shape)} for Hq={Hq} Hkv={Hkv} H={H}")
+    dev = x.device
+    q = torch.empty(B, Hq, S, 128, device=dev, dtype=_BF16)
+    k = torch.empty(B, Hkv, S, 128, device=dev, dtype=_BF16)
+    v = torch.empty(B, Hkv, S, 128, device=dev, dtype=_BF16)
+    ws = torch.empty(2 * B * S * 64, device=dev, dtype=torch.float32)
+    with torch.cuda.device(dev):
+        _lib.call("q35_qkv_proj_norm_rope", x.data_ptr(), w_qkv.data_ptr(), q_w.data_ptr(),
+                  k_w.data_ptr(), pos.data_ptr(), inv.data_ptr(), _lib.sections_arg(mrope_section),
+                  1 if interleaved else 0, q.data_ptr(), k.data_ptr(), v.data_ptr(), B, S, H, Hq,
+                  Hkv, float(eps), ws.data_ptr(), _stream(x))
     return q, k, v
 
 

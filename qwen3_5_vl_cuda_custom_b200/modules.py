@@ -207,6 +207,10 @@ class CudaFullAttention(nn.Module):
         self.k_norm = CudaRMSNorm(self.head_dim, eps=rms_norm_eps)
         self._qkv_cache: tuple | None = None
 
+    # prefill (>= 256 tokens, head_dim 128): QK-norm + mRoPE in the projection
+    # GEMM's epilogue instead of a separate pass over the bf16 projection
+    fuse_qkv_epilogue = True
+
     def _qkv_weight(self) -> tuple[torch.Tensor, torch.Tensor | None]:
         """Concatenated (q; k; v) projection weight (and bias), rebuilt whenever a
         source parameter is replaced or modified in place."""
@@ -225,11 +229,16 @@ class CudaFullAttention(nn.Module):
         Hq, Hkv, D = self.num_heads, self.num_kv_heads, self.head_dim
         if isinstance(mrope_apply, BoundMRoPE):
             w, b = self._qkv_weight()
-            qkv = K.matmul(x, w, b)
             rot = mrope_apply.rotary
             pos = mrope_apply.position_ids
             if pos.shape != (3, B, S):
                 raise RuntimeError(f"position_ids must be (3, {B}, {S}), got {tuple(pos.shape)}")
+            if (self.fuse_qkv_epilogue and D == 128 and b is None and (Hq + 2 * Hkv) % 2 == 0
+                    and B * S >= 256 and x.shape[-1] % 8 == 0):
+                return K.qkv_proj_norm_rope(x, w, self.q_norm.weight, self.k_norm.weight, pos,
+                                            rot.inv_freq, rot.mrope_section, Hq, Hkv,
+                                            self.q_norm.eps, rot.interleaved)
+            qkv = K.matmul(x, w, b)
             return K.qknorm_mrope(qkv, self.q_norm.weight, self.k_norm.weight, pos, rot.inv_freq,
                                   rot.mrope_section, B, S, Hq, Hkv, D, self.q_norm.eps,
                                   rot.interleaved)

@@ -287,6 +287,38 @@ def test_qknorm_mrope(D, sections, multimodal, interleaved):
         assert (got.float().cpu() - ref).abs().max() <= 2 ** -7 * ref.abs().max() + 1e-3
 
 
+@pytest.mark.parametrize("B,S,H,Hq,Hkv,sections,multimodal,interleaved", [
+    (2, 384, 512, 8, 2, [24, 20, 20], False, False),
+    (1, 300, 256, 4, 1, [24, 20, 20], True, False),   # ragged last row tile, MQA
+    (2, 256, 2048, 32, 4, [24, 20, 20], True, True),  # A3B head layout
+    (3, 100, 136, 6, 2, [16, 24, 24], False, False),  # K tail (136 = 2*64 + 8)
+])
+def test_qkv_proj_norm_rope(B, S, H, Hq, Hkv, sections, multimodal, interleaved):
+    """Projection GEMM with QK-norm + mRoPE + head-major split in its epilogue
+    vs the oracle's fp32 projection, RMSNorm and rotation (REF
+    modules/attention.py:82-87)."""
+    from qwen3_5_vl_cuda_custom_b200 import synthetic as syn
+    D = 128
+    g = gen(B * S + H)
+    x = bf(torch.randn(B, S, H, generator=g))
+    w = bf(torch.randn((Hq + 2 * Hkv) * D, H, generator=g) * H ** -0.5)
+    qw = bf(1 + 0.1 * torch.randn(D, generator=g))
+    kw = bf(1 + 0.1 * torch.randn(D, generator=g))
+    pos = syn.multimodal_positions(B, S) if multimodal else syn.text_positions(B, S, start=3000)
+    inv = O.inv_freq(D, 5e6)
+    q, k, v = K().qkv_proj_norm_rope(x.to(DEV), w.to(DEV), qw.to(DEV), kw.to(DEV), pos.to(DEV),
+                                     inv.to(DEV), sections, Hq, Hkv, 1e-6, interleaved)
+    xp = (x.float().reshape(B * S, H) @ w.float().t()).view(B, S, Hq + 2 * Hkv, D)
+    cos3, sin3 = O.mrope_cos_sin(pos, inv)
+    cos, sin = O.mrope_select(cos3, sin3, sections, interleaved)
+    qr = O.rotate(O.rmsnorm(xp[:, :, :Hq], qw, 1e-6).transpose(1, 2), cos, sin)
+    kr = O.rotate(O.rmsnorm(xp[:, :, Hq:Hq + Hkv], kw, 1e-6).transpose(1, 2), cos, sin)
+    vr = xp[:, :, Hq + Hkv:].transpose(1, 2)
+    for got, ref in ((q, qr), (k, kr), (v, vr)):
+        st = O.error_stats(got.float().cpu(), ref)
+        assert st["max_abs_over_bf16"] <= 2e-2 and st["mean_rel"] <= 5e-3, st
+
+
 def test_mrope_op_matches_oracle():
     from qwen3_5_vl_cuda_custom_b200 import synthetic as syn
     B, H, S, D = 2, 4, 400, 128
