@@ -57,6 +57,34 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return x < -126.f ? 0.f : r;
 }
 
+// Paired exp2 on the FMA pipes for two scores at once (Blackwell f32x2
+// arithmetic): x = i + f with i = round-to-nearest(x) (the 1.5 * 2^23 shift
+// trick), f in [-0.5, 0.5], 2^f from a degree-3 polynomial fitted to 2^f on
+// that interval (iteratively reweighted least squares on the relative error,
+// max relative error 7.5e-5), and i added to the exponent field of the result.
+// Inputs are clamped at -125 so the exponent field never underflows.
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 shift = make_float2(12582912.f, 12582912.f);
+  const float2 xr = __fadd2_rn(x, shift);                     // 1.5*2^23 + i
+  const float2 xi = __fadd2_rn(xr, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(xi, make_float2(-1.f, -1.f), x);  // x - i
+  float2 p = __ffma2_rn(make_float2(0.05517146f, 0.05517146f), f,
+                        make_float2(0.24261086f, 0.24261086f));
+  p = __ffma2_rn(p, f, make_float2(0.69326097f, 0.69326097f));
+  p = __ffma2_rn(p, f, make_float2(0.99992812f, 0.99992812f));
+  // the low mantissa bits of xr hold i; shifted by 23 they are i * 2^23 (mod 2^32)
+  return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(xr.x) << 23)),
+                     __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(xr.y) << 23)));
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 struct AttnParams {
   int Hq, Hkv;
   int64_t Sq, Skv;
@@ -516,10 +544,16 @@ __global__ void __launch_bounds__(kThreads2, 1)
         for (int c = 0; c < kTile; ++c)
           if (n0 + c > lim_c) sr[c] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      // row max: four independent 3-input max chains
+      float mx0 = m_used, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < kTile; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
-      const float m_new = fmaxf(m_used, mx);
+      for (int c = 0; c < kTile; c += 8) {
+        mx0 = max3f(mx0, __uint_as_float(sr[c]), __uint_as_float(sr[c + 1]));
+        mx1 = max3f(mx1, __uint_as_float(sr[c + 2]), __uint_as_float(sr[c + 3]));
+        mx2 = max3f(mx2, __uint_as_float(sr[c + 4]), __uint_as_float(sr[c + 5]));
+        mx3 = max3f(mx3, __uint_as_float(sr[c + 6]), __uint_as_float(sr[c + 7]));
+      }
+      const float m_new = max3f(mx0, mx1, fmaxf(mx2, mx3));
       bool need = false;
       float alpha = 1.f;
       if (j == 0 || m_used == -INFINITY) {
@@ -531,7 +565,35 @@ __global__ void __launch_bounds__(kThreads2, 1)
         l *= alpha;
       }
       const float mus = ((m_used == -INFINITY) ? 0.f : m_used) * p.sl2;
-      // PV(j-1) is complete (it precedes S(j) in the tensor pipe): O may be scaled.
+      // exponentials, bf16 P over the first 64 S columns.  Score pairs are
+      // scaled with one f32x2 FMA; pairs alternate between the MUFU unit
+      // (ex2.approx) and the paired FMA polynomial; row sums in f32x2.
+      const float2 sl2v = make_float2(p.sl2, p.sl2), nmus = make_float2(-mus, -mus);
+      float2 lsum0 = make_float2(0.f, 0.f), lsum1 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int qtr = 0; qtr < 4; ++qtr) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 sv = make_float2(__uint_as_float(sr[qtr * 32 + 2 * i]),
+                                        __uint_as_float(sr[qtr * 32 + 2 * i + 1]));
+          const float2 x = __ffma2_rn(sv, sl2v, nmus);
+          float2 e;
+          if (i & 1) {
+            e = exp2_fma2(x);
+          } else {
+            e.x = exp2_mufu(x.x);
+            e.y = exp2_mufu(x.y);
+          }
+          if (i & 2) lsum1 = __fadd2_rn(lsum1, e);
+          else lsum0 = __fadd2_rn(lsum0, e);
+          pk[i] = pack_bf2(e.x, e.y);
+        }
+        sm100::tmem_st16(s_tm + qtr * 16, pk);
+      }
+      l += (lsum0.x + lsum0.y) + (lsum1.x + lsum1.y);
+      // PV(j-1) is complete (it precedes S(j) in the tensor pipe): O may be scaled
+      // (after the exponentials, when the score registers are free).
       if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
@@ -542,19 +604,6 @@ __global__ void __launch_bounds__(kThreads2, 1)
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
           sm100::tmem_st32(o_tm + c * 32, r);
         }
-      }
-      // exponentials, bf16 P over the first 64 S columns
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float a = exp2_mufu(fmaf(__uint_as_float(sr[half * 64 + 2 * i]), p.sl2, -mus));
-          const float b2 = exp2_fma(fmaf(__uint_as_float(sr[half * 64 + 2 * i + 1]), p.sl2, -mus));
-          l += a + b2;
-          pk[i] = pack_bf2(a, b2);
-        }
-        sm100::tmem_st32(s_tm + half * 32, pk);
       }
       sm100::tmem_wait_st();
       sm100::tc_fence_before();
@@ -568,7 +617,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
         report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 327, n_tiles, row);
       } else {
         sm100::tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
+        // a row that saw no unmasked key (m_used still -inf) is all zeros; its
+        // l holds only the polynomial's 2^-125 floor for masked scores
+        const float inv = (l > 0.f && m_used != -INFINITY) ? 1.f / l : 0.f;
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
@@ -592,7 +643,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
     if (valid && p.lse)
       p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.Sq + qi] =
-          l > 0.f ? m_used * p.scale + logf(l) : -INFINITY;
+          (l > 0.f && m_used != -INFINITY) ? m_used * p.scale + logf(l) : -INFINITY;
   }
 
   sm100::tc_fence_before();
