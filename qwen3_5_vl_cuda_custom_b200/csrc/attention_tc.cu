@@ -24,6 +24,7 @@
 // Every mbarrier wait is bounded (sm100::mbar_wait); on timeout the kernel
 // records DEV_ERR_WAIT_TIMEOUT and unwinds.
 #include "sm100.cuh"
+#include <cstdlib>
 
 namespace q35 {
 namespace {
@@ -363,15 +364,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 // issued only after PV_h(j), which reads P_h(j) from the same columns, and
 // tensor operations of one thread complete in issue order, so the commit that
 // announces S_h(j+1) also guarantees PV_h(j) has finished (O_h may then be
-// rescaled without another wait).  Softmax reads S twice from TMEM (row max,
-// then exponentials) to stay within ~200 registers with 10 warps.
-constexpr int kThreads2 = 320;
+// rescaled without another wait).
+// 384 threads = three warpgroups: WG0 (warp 0 TMA, warp 1 MMA, warps 2-3
+// idle) drops to 88 registers per thread with setmaxnreg and the two softmax
+// warpgroups (warps 4-7 head a, 8-11 head b) rise to 208, enough to hold a
+// whole 128-score row without spilling.  The split uses exactly the launch
+// allocation: 128 * 88 + 256 * 208 = 384 * 168 (the kernel must be built with
+// 168 registers per thread, which 384 threads and one CTA per SM give).
+constexpr int kThreads2 = 384;
+constexpr int kRegsLaunch2 = 168, kRegsCtl2 = 88, kRegsSoftmax2 = 208;
+static_assert(128 * kRegsCtl2 + 256 * kRegsSoftmax2 <= kThreads2 * kRegsLaunch2,
+              "setmaxnreg split exceeds the launch register allocation");
 constexpr int kQ2Off = 0;                          // Q_a, Q_b: 2 x 2 halves
 constexpr int kK2Off = kQ2Off + 4 * kHalfBytes;    // K: 2 stages x 2 halves
 constexpr int kV2Off = kK2Off + 4 * kHalfBytes;    // V: 2 stages x 2 halves
 constexpr int kBar2Off = kV2Off + 4 * kHalfBytes;
-constexpr int kSmem2 = 1024 + kBar2Off + 16 * 8;
+constexpr int kSmem2 = 1024 + kBar2Off + 20 * 8;
 
+// Pairs (of every 8) whose exponentials use the FMA polynomial instead of MUFU.
+template <int kPoly>
+constexpr uint32_t kPolyPattern() {
+  return kPoly == 2 ? 0x22u : kPoly == 3 ? 0x52u : kPoly == 4 ? 0xAAu : kPoly == 5 ? 0xADu : 0x00u;
+}
+
+template <int kPoly>
 __global__ void __launch_bounds__(kThreads2, 1)
     attn_tc2_kernel(const __grid_constant__ CUtensorMap tmQ,
                     const __grid_constant__ CUtensorMap tmK,
@@ -380,14 +396,18 @@ __global__ void __launch_bounds__(kThreads2, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kBar2Off);
+  // K and V tiles have separate rings: K(j) is free once both S MMAs of
+  // tile j are done, a cycle before the PV MMAs release V(j).
   uint64_t *q_full = bars + 0;
-  uint64_t *kv_full = bars + 1;   // [2]
-  uint64_t *kv_empty = bars + 3;  // [2]
+  uint64_t *k_full = bars + 1;    // [2]
+  uint64_t *k_empty = bars + 3;   // [2]
   uint64_t *s_full = bars + 5;    // [2] per head
   uint64_t *p_full = bars + 7;    // [2] per head
   uint64_t *o_done = bars + 9;
   uint64_t *drain = bars + 10;
   uint32_t *s_tmem = reinterpret_cast<uint32_t *>(bars + 12);
+  uint64_t *v_full = bars + 13;   // [2]
+  uint64_t *v_empty = bars + 15;  // [2]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // 1-D grid, heaviest query blocks (most causal key tiles) first across all
@@ -408,8 +428,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
   if (threadIdx.x == 0) {
     sm100::mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      sm100::mbar_init(&kv_full[i], 1);
-      sm100::mbar_init(&kv_empty[i], 1);
+      sm100::mbar_init(&k_full[i], 1);
+      sm100::mbar_init(&k_empty[i], 1);
+      sm100::mbar_init(&v_full[i], 1);
+      sm100::mbar_init(&v_empty[i], 1);
       sm100::mbar_init(&s_full[i], 1);
       sm100::mbar_init(&p_full[i], 128);
     }
@@ -426,6 +448,8 @@ __global__ void __launch_bounds__(kThreads2, 1)
   sm100::tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
+  if (warp < 4) {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegsCtl2));
   if (warp == 0 && lane == 0 && n_tiles > 0) {
     // ------------------------------------------------ TMA producer
     sm100::mbar_arrive_expect_tx(q_full, 4 * kHalfBytes);
@@ -436,18 +460,24 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
     for (int j = 0; j < n_tiles; ++j) {
       const int st = j & 1;
-      if (!sm100::mbar_wait(&kv_empty[st], ((j >> 1) & 1) ^ 1)) {
-        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 321, j, 0);
-        break;
-      }
+      const uint32_t ph = ((j >> 1) & 1) ^ 1;
       uint8_t *sk = smem + kK2Off + st * 2 * kHalfBytes;
       uint8_t *sv = smem + kV2Off + st * 2 * kHalfBytes;
       const int32_t r = kv_row + j * kTile;
-      sm100::mbar_arrive_expect_tx(&kv_full[st], 4 * kHalfBytes);
-      sm100::tma_load_2d(sk, &tmK, &kv_full[st], 0, r);
-      sm100::tma_load_2d(sk + kHalfBytes, &tmK, &kv_full[st], 64, r);
-      sm100::tma_load_2d(sv, &tmV, &kv_full[st], 0, r);
-      sm100::tma_load_2d(sv + kHalfBytes, &tmV, &kv_full[st], 64, r);
+      if (!sm100::mbar_wait(&k_empty[st], ph)) {
+        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 321, j, 0);
+        break;
+      }
+      sm100::mbar_arrive_expect_tx(&k_full[st], 2 * kHalfBytes);
+      sm100::tma_load_2d(sk, &tmK, &k_full[st], 0, r);
+      sm100::tma_load_2d(sk + kHalfBytes, &tmK, &k_full[st], 64, r);
+      if (!sm100::mbar_wait(&v_empty[st], ph)) {
+        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 328, j, 0);
+        break;
+      }
+      sm100::mbar_arrive_expect_tx(&v_full[st], 2 * kHalfBytes);
+      sm100::tma_load_2d(sv, &tmV, &v_full[st], 0, r);
+      sm100::tma_load_2d(sv + kHalfBytes, &tmV, &v_full[st], 64, r);
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------ MMA issuer
@@ -473,6 +503,10 @@ __global__ void __launch_bounds__(kThreads2, 1)
       sm100::mma_commit(&s_full[hh]);
     };
     auto issue_pv = [&](int hh, int i) -> bool {
+      if (hh == 0 && !sm100::mbar_wait(&v_full[i & 1], (i >> 1) & 1)) {
+        report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 329, i, hh);
+        return false;
+      }
       if (!sm100::mbar_wait(&p_full[hh], i & 1)) {
         report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 323, i, hh);
         return false;
@@ -490,7 +524,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     };
     for (int j = 0; j < n_tiles && ok; ++j) {
       const int st = j & 1;
-      if (!sm100::mbar_wait(&kv_full[st], (j >> 1) & 1)) {
+      if (!sm100::mbar_wait(&k_full[st], (j >> 1) & 1)) {
         report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 324, j, 0);
         ok = false;
         break;
@@ -500,21 +534,24 @@ __global__ void __launch_bounds__(kThreads2, 1)
       issue_s(0, j);
       if (j > 0) {
         if (!issue_pv(1, j - 1)) { ok = false; break; }
-        sm100::mma_commit(&kv_empty[(j - 1) & 1]);
+        sm100::mma_commit(&v_empty[(j - 1) & 1]);
       }
       issue_s(1, j);
+      sm100::mma_commit(&k_empty[st]);
     }
     if (ok) {
       if (issue_pv(0, n_tiles - 1) && issue_pv(1, n_tiles - 1)) {
-        sm100::mma_commit(&kv_empty[(n_tiles - 1) & 1]);
+        sm100::mma_commit(&v_empty[(n_tiles - 1) & 1]);
         sm100::mma_commit(o_done);
       }
     }
     sm100::mma_commit(drain);
     if (!sm100::mbar_wait(drain, 0)) report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 325, 0, 0);
-  } else if (warp >= 2) {
+  }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsSoftmax2));
     // ------------------------------------------------ softmax, one group per head
-    const int hh = (warp - 2) >> 2;          // warps 2-5: head a, 6-9: head b
+    const int hh = (warp - 4) >> 2;          // warps 4-7: head a, 8-11: head b
     const int q = warp & 3;                  // TMEM lane quadrant of this warp
     const int row = q * 32 + lane;
     const int64_t qi = m0 + row;
@@ -579,7 +616,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
                                         __uint_as_float(sr[qtr * 32 + 2 * i + 1]));
           const float2 x = __ffma2_rn(sv, sl2v, nmus);
           float2 e;
-          if (i & 1) {
+          if (((kPolyPattern<kPoly>() >> (i & 7)) & 1u)) {
             e = exp2_fma2(x);
           } else {
             e.x = exp2_mufu(x.x);
@@ -692,9 +729,28 @@ int q35_attn_prefill_tc(const void *q, const void *k, const void *v, void *out,
   p.err = err;
   if ((Hq / Hkv) % 2 == 0) {
     // GQA with an even group: two heads per CTA share each K/V tile.
-    { const int _st = ensure_smem_attr(reinterpret_cast<const void *>(attn_tc2_kernel), kSmem2); if (_st) return _st; }
     dim3 grid2(static_cast<unsigned>(p.n_mblocks * B * Hq / 2));
-    attn_tc2_kernel<<<grid2, kThreads2, kSmem2, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+    const char *ev = getenv("Q35_ATTN_POLY");
+    const int np = ev ? atoi(ev) : 3;
+    auto go = [&](auto kern) -> int {
+      const int st2 = ensure_smem_attr(reinterpret_cast<const void *>(kern), kSmem2);
+      if (st2) return st2;
+      // the setmaxnreg split assumes exactly kRegsLaunch2 registers at launch
+      static thread_local int regs_ok[8] = {0};
+      if (!regs_ok[np & 7]) {
+        cudaFuncAttributes fa;
+        const cudaError_t fe = cudaFuncGetAttributes(&fa, reinterpret_cast<const void *>(kern));
+        if (fe != cudaSuccess) return cuda_fail(fe, "attn_prefill_tc2: cudaFuncGetAttributes");
+        if (fa.numRegs != kRegsLaunch2)
+          return fail(Q35_ERR_UNSUPPORTED, "attn_prefill_tc2 built with %d registers per thread, "
+                      "the register split needs %d", fa.numRegs, kRegsLaunch2);
+        regs_ok[np & 7] = 1;
+      }
+      kern<<<grid2, kThreads2, kSmem2, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
+      return 0;
+    };
+    int st3 = np == 2 ? go(attn_tc2_kernel<2>) : np == 3 ? go(attn_tc2_kernel<3>) : np == 5 ? go(attn_tc2_kernel<5>) : go(attn_tc2_kernel<4>);
+    if (st3) return st3;
     Q35_LAUNCH_CHECK("attn_prefill_tc2 launch");
     return Q35_OK;
   }
