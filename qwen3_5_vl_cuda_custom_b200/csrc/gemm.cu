@@ -93,6 +93,7 @@ struct TileInfo {
   int group;
   int nt;          // n-tile index
   int split;       // K split (dense split-K), else 0
+  int half;        // pair tile of 128 rows (64 per CTA, M = 128 MMA)
 };
 
 __device__ __forceinline__ TileInfo decode_tile(int tile, const GemmParams &p,
@@ -424,10 +425,15 @@ struct PairLayout {
   static constexpr int bytes(int E) { return 1024 + kGroupOff + 2 * (E + 1) * 4; }
 };
 
+__device__ __forceinline__ bool pair_half_ok(const GemmParams &p) {
+  return !p.b_packed && !p.bias && !p.residual && !p.out_f32;
+}
+
 __device__ __forceinline__ TileInfo decode_pair_tile(int tile, const GemmParams &p,
                                                      const int *s_off, const int *s_pt) {
   TileInfo ti;
   ti.split = 0;
+  ti.half = 0;
   if (p.offsets == nullptr) {
     // Rasterise in bands of 8 M tiles: CTAs running together share 8 A tiles
     // and a run of B tiles in L2, whatever the aspect ratio of the problem.
@@ -456,13 +462,19 @@ __device__ __forceinline__ TileInfo decode_pair_tile(int tile, const GemmParams 
   ti.group = e;
   ti.row0 = s_off[e] + mt * 256;
   ti.rows_valid = min(256, s_off[e + 1] - ti.row0);
+  // A group's last <= 128 rows run as an M = 128 pair MMA (half the tensor
+  // time of a padded 256-row tile).  Plain stores or SwiGLU, unpacked B only.
+  ti.half = (ti.rows_valid <= 128 && pair_half_ok(p)) ? 1 : 0;
   return ti;
 }
+
+
 
 template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                     const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+                     const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmB64, GemmParams p) {
   using L = PairLayout;
   constexpr int BN = 256;
   constexpr int S = L::kStages;
@@ -527,9 +539,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int tile = pair; tile < total && ok; tile += npairs) {
       const TileInfo ti = decode_pair_tile(tile, p, s_off, s_pt);
-      const int arow = ti.row0 + static_cast<int>(rank) * 128;
+      const int arow = ti.row0 + static_cast<int>(rank) * (ti.half ? 64 : 128);
       const int brow = ti.group * p.b_rows_per_group + ti.nt * p.b_tile_step +
                        static_cast<int>(rank) * p.b_second_off;
+      // SwiGLU half tile: each CTA's B half holds 64 gate rows and the
+      // matching 64 up rows, so every accumulator lane gets gate and up
+      const bool split_b = EPI == EPI_SWIGLU && ti.half;
+      const int brow_g = ti.group * p.b_rows_per_group + ti.nt * p.b_tile_step +
+                         static_cast<int>(rank) * 64;
       for (int kb = 0; kb < k_blocks; ++kb, ++g) {
         const int st = g % S;
         const uint32_t ph = (g / S) & 1u;
@@ -543,19 +560,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t leader_full = sm100::mapa_shared(sm100::smem_u32(&full[st]), 0);
         if (rank == 0) sm100::mbar_arrive_expect_tx(&full[st], 2 * L::kStageBytes);
         sm100::tma_load_2d_pair(sa, &tmA, leader_full, kb * kBK, arow);
-        if (p.b_packed)  // tile (brow / 128, kb) is 16 KB contiguous
+        if (split_b) {
+          sm100::tma_load_2d_pair(sb, &tmB64, leader_full, kb * kBK, brow_g);
+          sm100::tma_load_2d_pair(sb + L::kHalf / 2, &tmB64, leader_full, kb * kBK,
+                                  brow_g + p.b_second_off);
+        } else if (p.b_packed) {  // tile (brow / 128, kb) is 16 KB contiguous
           sm100::tma_load_2d_pair(sb, &tmB, leader_full, 0, ((brow >> 7) * k_blocks + kb) * 128);
-        else
+        } else {
           sm100::tma_load_2d_pair(sb, &tmB, leader_full, kb * kBK, brow);
+        }
       }
     }
   } else if (warp == 1 && lane == 0 && rank == 0) {
     // ------------------------------------------------ MMA issuer (leader CTA)
-    constexpr uint32_t idesc = sm100::idesc_bf16_f32(256, BN);
+    constexpr uint32_t idesc256 = sm100::idesc_bf16_f32(256, BN);
+    constexpr uint32_t idesc128 = sm100::idesc_bf16_f32(128, BN);
     uint32_t g = 0, j = 0;
     bool ok = true;
     for (int tile = pair; tile < total && ok; tile += npairs, ++j) {
       const uint32_t acc = j & 1u, use = j >> 1;
+      const uint32_t idesc = decode_pair_tile(tile, p, s_off, s_pt).half ? idesc128 : idesc256;
       if (!sm100::mbar_wait(&tempty[acc], (use & 1u) ^ 1u)) {
         report_error(p.err, DEV_ERR_WAIT_TIMEOUT, 212, tile, 0);
         break;
@@ -600,7 +624,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       const bool valid = r_in_tile < ti.rows_valid;
       const int64_t row = static_cast<int64_t>(ti.row0) + r_in_tile;
-      if constexpr (EPI == EPI_PLAIN) {
+      if (EPI != EPI_QKV && ti.half) {
+        // M = 128 pair accumulator: lane l < 64 holds row 64 * rank + l, tile
+        // columns [0, 128); lane 64 + l the same row, columns [128, 256).
+        const int tl = q * 32 + lane;
+        const int rh = static_cast<int>(rank) * 64 + (tl & 63);
+        const int upper = tl >> 6;
+        const bool valid_h = rh < ti.rows_valid;
+        const int64_t row_h = static_cast<int64_t>(ti.row0) + rh;
+        if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            uint32_t rg[32], ru[32];
+            sm100::tmem_ld32(t_row + c * 32, rg);
+            sm100::tmem_ld32(t_row + 64 + c * 32, ru);
+            sm100::tmem_wait_ld();
+            const int col = ti.nt * (BN / 2) + upper * 64 + c * 32;
+            if (valid_h && col < p.N) {
+              float v[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                v[i] = silu(__uint_as_float(rg[i])) * __uint_as_float(ru[i]);
+              store32(p.out + row_h * p.ldo + col, v);
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            sm100::tmem_ld32(t_row + c * 32, r);
+            sm100::tmem_wait_ld();
+            const int col = ti.nt * BN + upper * 128 + c * 32;
+            if (valid_h && col < p.N) {
+              float v[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+              store32(p.out + row_h * p.ldo + col, v);
+            }
+          }
+        }
+      } else if constexpr (EPI == EPI_PLAIN) {
         const int n0 = ti.nt * BN;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -754,7 +817,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int EPI>
 int launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmParams &p,
-                     int max_pair_tiles, cudaStream_t s) {
+                     int max_pair_tiles, cudaStream_t s, const CUtensorMap *tb64 = nullptr) {
   const int smem = PairLayout::bytes(p.E);
   auto kern = gemm_pair_kernel<EPI>;
   { const int _st = ensure_smem_attr(reinterpret_cast<const void *>(kern), smem); if (_st) return _st; }
@@ -771,7 +834,7 @@ int launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmPar
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  Q35_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, p));
+  Q35_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, tb64 ? *tb64 : tb, p));
   return Q35_OK;
 }
 
@@ -1074,7 +1137,15 @@ static int grouped_common(const void *a, const void *w, void *out,
   const int64_t max_pair = ((rows_cap + 255) / 256 + E) * p.n_tiles;
   const int mp = static_cast<int>(max_pair < (1 << 30) ? max_pair : (1 << 30));
   (void)mt;
-  if (swiglu) return launch_gemm_pair<EPI_SWIGLU>(ta, tb, p, mp, s);
+  if (swiglu) {
+    // 64-row B boxes for the gate/up halves of M = 128 pair tiles
+    CUtensorMap tb64 = tb;
+    if (!packed) {
+      st = make_tmap_bf16_2d(&tb64, w, K, static_cast<uint64_t>(E) * b_rows_per_group, K * 2, kBK, 64);
+      if (st) return st;
+    }
+    return launch_gemm_pair<EPI_SWIGLU>(ta, tb, p, mp, s, &tb64);
+  }
   return launch_gemm_pair<EPI_PLAIN>(ta, tb, p, mp, s);
 }
 

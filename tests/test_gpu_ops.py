@@ -199,6 +199,42 @@ def test_permutation_skewed_zipf():
 
 
 # ------------------------------------------------------------------ grouped GEMMs + combine
+@pytest.mark.parametrize("H,I", [(256, 128), (512, 192)])
+def test_grouped_gemm_ragged_groups(H, I):
+    """Group sizes around the 128/256-row tile edges: a group's last <= 128
+    rows run as an M = 128 CTA-pair tile, larger remainders as 256-row tiles.
+    Both grouped GEMMs against fp32 per-group products."""
+    counts = [1, 64, 127, 128, 129, 200, 255, 256, 257, 300, 0, 384, 385, 520]
+    E = len(counts)
+    g = gen(H + I)
+    idx = torch.cat([torch.full((c,), e, dtype=torch.int32) for e, c in enumerate(counts)])
+    idx = idx[torch.randperm(idx.numel(), generator=g)].reshape(-1, 1)
+    T = idx.shape[0]
+    x = bf(torch.randn(T, H, generator=g))
+    gu = bf(torch.randn(E, 2 * I, H, generator=g) * 0.05)
+    dn = bf(torch.randn(E, H, I, generator=g) * 0.05)
+    Kk = K()
+    perm = Kk.moe_permute(idx.to(DEV), E)
+    xs = Kk.gather_rows(x.to(DEV), perm.sorted_tok)
+    act = Kk.grouped_gateup_swiglu(xs, gu.to(DEV), perm)
+    y = Kk.grouped_down(act, dn.to(DEV), perm)
+    off = perm.offsets.cpu().long().tolist()
+    xs_c = xs.float().cpu()
+    act_c = act.float().cpu()
+    for e in range(E):
+        a, b = off[e], off[e + 1]
+        assert b - a == counts[e]
+        if a == b:
+            continue
+        h = xs_c[a:b] @ gu[e].float().t()
+        ref_act = torch.nn.functional.silu(h[:, :I]) * h[:, I:]
+        st = O.error_stats(act_c[a:b], ref_act)
+        assert st["max_abs_over_bf16"] <= 2e-2 and st["mean_rel"] <= 5e-3, (e, counts[e], st)
+        ref_y = act_c[a:b] @ dn[e].float().t()
+        st = O.error_stats(y[a:b].float().cpu(), ref_y)
+        assert st["max_abs_over_bf16"] <= 2e-2 and st["mean_rel"] <= 5e-3, (e, counts[e], st)
+
+
 @pytest.mark.parametrize("T,H,I,E,k", [(128, 256, 128, 16, 4), (1024, 2048, 768, 128, 8),
                                        (37, 256, 64, 8, 2), (512, 512, 96, 32, 4),
                                        (64, 256, 96, 4, 2)])
