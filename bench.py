@@ -217,7 +217,8 @@ def staged_forward(layer, rot, x, pos, marks=None):
     return out.reshape(B, S, H)
 
 
-LAUNCHES_PER_LAYER = 15  # rmsnorm, rope table, qkv+norm+rope, attn, o, rmsnorm, router, permute x3, gather, gu, down, combine
+LAUNCHES_PER_LAYER = 16  # rmsnorm, rope table, qkv+norm+rope, attn, o, rmsnorm, router logits,
+# router top-k, permute x3 (count, scan, scatter), gather, gate_up, down, combine
 
 
 def cpu_reference_step_fn(cfg, P, x_cpu, pos_cpu, dtype):
