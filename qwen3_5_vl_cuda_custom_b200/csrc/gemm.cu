@@ -975,7 +975,9 @@ extern "C" int q35_router_logits_tc(const void *x, const void *w3,
   if (T == 0) return Q35_OK;
   int *err = device_error_word();
   if (!err) return fail(Q35_ERR_CUDA, "router_logits_tc: no device error word");
-  constexpr int BN = 64;
+  // One 128-wide N tile when E allows (x and its three planes cross L2 once),
+  // else 64-wide tiles.
+  const int BN = E % 128 == 0 ? 128 : 64;
   CUtensorMap ta, tb;
   int st = make_tmap_bf16_2d(&ta, x, H, T, static_cast<uint64_t>(H) * 2, kBK, kBM);
   if (st) return st;
@@ -999,7 +1001,9 @@ extern "C" int q35_router_logits_tc(const void *x, const void *w3,
   p.k_splits = k_splits;
   p.split_stride = T * static_cast<int64_t>(E);
   const int tiles = static_cast<int>(((T + kBM - 1) / kBM) * p.n_tiles * k_splits);
-  return launch_gemm<BN, EPI_PLAIN, 8>(ta, tb, p, tiles, reinterpret_cast<cudaStream_t>(stream));
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  if (BN == 128) return launch_gemm<128, EPI_PLAIN, 6>(ta, tb, p, tiles, cs);
+  return launch_gemm<64, EPI_PLAIN, 8>(ta, tb, p, tiles, cs);
 }
 
 // Re-lays a K-major bf16 matrix [rows, K] (e.g. all experts' weights,
