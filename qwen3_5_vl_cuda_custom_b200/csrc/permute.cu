@@ -66,11 +66,18 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(
   const int e = threadIdx.x;
   int32_t run = 0;
   if (e < E) {
-    for (int64_t c = 0; c < n_chunks; ++c) {
-      int32_t *p = chunk_counts + c * E + e;
-      const int32_t v = *p;
-      *p = run;  // becomes the chunk's base within expert e
-      run += v;
+    // 16 chunk counts loaded at a time (independent loads), then rewritten
+    // as each chunk's base within expert e
+    for (int64_t c0 = 0; c0 < n_chunks; c0 += 16) {
+      int32_t v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        v[i] = (c0 + i < n_chunks) ? chunk_counts[(c0 + i) * E + e] : 0;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (c0 + i < n_chunks) chunk_counts[(c0 + i) * E + e] = run;
+        run += v[i];
+      }
     }
     counts[e] = run;
   }
@@ -141,10 +148,14 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(
 
 // out[t,:] = residual[t,:] + sum_j w[t,j] * y[slot_pos[t*k+j],:]  (fp32 sum,
 // slot order, one rounding).  One CTA per token, 8 columns per thread-step.
+// KF > 0: k == KF known at compile time; the KF row loads of a column
+// block are issued together before the (unchanged, slot-ordered) sum.
+template <int KF>
 __global__ void __launch_bounds__(256) combine_kernel(
     const uint16_t *__restrict__ y, const float *__restrict__ w,
     const int32_t *__restrict__ slot_pos, const void *__restrict__ residual,
-    int residual_f32, uint16_t *__restrict__ out, int k, int64_t H) {
+    int residual_f32, uint16_t *__restrict__ out, int k_dyn, int64_t H) {
+  const int k = KF > 0 ? KF : k_dyn;
   const int64_t t = blockIdx.x;
   __shared__ int32_t s_pos[16];
   __shared__ float s_w[16];
@@ -158,18 +169,40 @@ __global__ void __launch_bounds__(256) combine_kernel(
     float acc[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) acc[q] = 0.f;
-    for (int j = 0; j < k; ++j) {
-      const int32_t p = s_pos[j];
-      if (p < 0) continue;
-      const uint4 u = *reinterpret_cast<const uint4 *>(y + static_cast<int64_t>(p) * H + c);
-      float v[8];
-      unpack_bf2(u.x, v[0], v[1]);
-      unpack_bf2(u.y, v[2], v[3]);
-      unpack_bf2(u.z, v[4], v[5]);
-      unpack_bf2(u.w, v[6], v[7]);
-      const float wj = s_w[j];
+    if constexpr (KF > 0) {
+      uint4 u[KF];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) acc[q] = fmaf(wj, v[q], acc[q]);
+      for (int j = 0; j < KF; ++j) {
+        const int32_t p = s_pos[j];
+        u[j] = p >= 0 ? *reinterpret_cast<const uint4 *>(y + static_cast<int64_t>(p) * H + c)
+                      : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int j = 0; j < KF; ++j) {
+        if (s_pos[j] < 0) continue;
+        float v[8];
+        unpack_bf2(u[j].x, v[0], v[1]);
+        unpack_bf2(u[j].y, v[2], v[3]);
+        unpack_bf2(u[j].z, v[4], v[5]);
+        unpack_bf2(u[j].w, v[6], v[7]);
+        const float wj = s_w[j];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] = fmaf(wj, v[q], acc[q]);
+      }
+    } else {
+      for (int j = 0; j < k; ++j) {
+        const int32_t p = s_pos[j];
+        if (p < 0) continue;
+        const uint4 u = *reinterpret_cast<const uint4 *>(y + static_cast<int64_t>(p) * H + c);
+        float v[8];
+        unpack_bf2(u.x, v[0], v[1]);
+        unpack_bf2(u.y, v[2], v[3]);
+        unpack_bf2(u.z, v[4], v[5]);
+        unpack_bf2(u.w, v[6], v[7]);
+        const float wj = s_w[j];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) acc[q] = fmaf(wj, v[q], acc[q]);
+      }
     }
     if (residual) {
       float v[8];
@@ -320,10 +353,15 @@ extern "C" int q35_moe_combine(const void *y, const float *weights,
   if (!aligned16(y) || !aligned16(out) || (residual && !aligned16(residual)))
     return fail(Q35_ERR_ALIGN, "moe_combine: pointers not 16-byte aligned");
   if (T == 0) return Q35_OK;
-  combine_kernel<<<static_cast<unsigned>(T), 256, 0,
-                   reinterpret_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint16_t *>(y), weights, slot_pos, residual,
-      residual_f32, static_cast<uint16_t *>(out), k, H);
+  cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+  if (k == 8)
+    combine_kernel<8><<<static_cast<unsigned>(T), 256, 0, cs>>>(
+        static_cast<const uint16_t *>(y), weights, slot_pos, residual, residual_f32,
+        static_cast<uint16_t *>(out), k, H);
+  else
+    combine_kernel<0><<<static_cast<unsigned>(T), 256, 0, cs>>>(
+        static_cast<const uint16_t *>(y), weights, slot_pos, residual, residual_f32,
+        static_cast<uint16_t *>(out), k, H);
   Q35_LAUNCH_CHECK("moe_combine launch");
   return Q35_OK;
 }
