@@ -42,7 +42,7 @@ sys.path.insert(0, str(ROOT))
 
 # DRAM bytes (read + write) per launch from `ncu --set full` captures of the C2
 # workload (profiles/grouped_gemm_pair_c2_full.md, profiles/attention_tc2_c2_full.md)
-TRAFFIC_BYTES_C2 = {"gate_up_swiglu": 990.0e6, "down": 596.8e6, "attention": 42.7e6}
+TRAFFIC_BYTES_C2 = {"gate_up_swiglu": 1055.5e6, "down": 575.9e6, "attention": 42.9e6}
 # algorithmic bytes of the same launches (weights + rows read, outputs written)
 ALGO_BYTES_C2 = {"gate_up_swiglu": 989.8e6, "down": 587.2e6, "attention": 75.5e6}
 LINK_GBS = 770.0  # measured NVLink peer copy per direction on this pool
