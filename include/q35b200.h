@@ -326,6 +326,30 @@ Q35_API int q35_attn_decode_fwd(const void *q, const void *k, const void *v, voi
                         int D, float scale, float *workspace,
                         q35_stream_t stream);
 
+/* Attention over a preallocated KV cache: k_cache / v_cache bf16
+ * [B, Hkv, kv_cap, D], of which the first Skv rows per head are valid; q and
+ * out as in q35_attn_prefill_fwd / q35_attn_decode_fwd (the same kernels with
+ * a head stride of kv_cap rows instead of Skv).  kv_cap >= Skv.  Rows past Skv
+ * are read by the last key tile and masked, so they must hold finite values
+ * (zero-initialise the cache).  Replaces the torch.cat of past and new K/V
+ * followed by flash_attention (REF modules/attention.py:89-95).            */
+Q35_API int q35_attn_prefill_cache_fwd(const void *q, const void *k_cache, const void *v_cache,
+                                       void *out, float *lse, int64_t B, int Hq, int Hkv,
+                                       int64_t Sq, int64_t Skv, int64_t kv_cap, int D,
+                                       float scale, int causal, q35_stream_t stream);
+Q35_API int q35_attn_decode_cache_fwd(const void *q, const void *k_cache, const void *v_cache,
+                                      void *out, int64_t B, int Hq, int Hkv, int64_t Sq,
+                                      int64_t Skv, int64_t kv_cap, int D, float scale,
+                                      float *workspace, q35_stream_t stream);
+
+/* In-place KV-cache append: rows s < S of k_new / v_new bf16 [B, Hkv, S, D]
+ * go to rows offset + s of the [B, Hkv, cap, D] caches.  offset + S <= cap,
+ * D % 8 == 0.  Replaces k = cat(past_k, k), v = cat(past_v, v)
+ * (REF modules/attention.py:89-93) without copying the past rows.         */
+Q35_API int q35_kv_append(const void *k_new, const void *v_new, void *k_cache, void *v_cache,
+                          int64_t B, int Hkv, int64_t S, int D, int64_t cap, int64_t offset,
+                          q35_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

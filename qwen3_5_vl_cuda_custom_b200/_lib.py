@@ -53,6 +53,14 @@ _SIGS = {
                               c_int64, c_void_p]),
     "q35_grouped_gemm_gateup_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                                c_int, c_int64, c_int, c_int, c_int, c_void_p]),
+    "q35_attn_prefill_cache_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                           c_int, c_int, c_int64, c_int64, c_int64, c_int, c_float,
+                                           c_int, c_void_p]),
+    "q35_attn_decode_cache_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int,
+                                          c_int64, c_int64, c_int64, c_int, c_float, c_void_p,
+                                          c_void_p]),
+    "q35_kv_append": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_int,
+                              c_int64, c_int64, c_void_p]),
     "q35_grouped_gemm_down": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                       c_int64, c_int, c_int, c_int, c_void_p]),
     "q35_pack_b_tiles": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p]),

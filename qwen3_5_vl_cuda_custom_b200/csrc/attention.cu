@@ -100,7 +100,7 @@ template <int D>
 __global__ void __launch_bounds__(kPThreads, 2) attn_prefill_kernel(
     const uint16_t *__restrict__ q, const uint16_t *__restrict__ k,
     const uint16_t *__restrict__ v, uint16_t *__restrict__ out,
-    float *__restrict__ lse, int Hq, int Hkv, int64_t Sq, int64_t Skv,
+    float *__restrict__ lse, int Hq, int Hkv, int64_t Sq, int64_t Skv, int64_t kv_cap,
     float scale_log2, float scale, int causal) {
   extern __shared__ __align__(128) uint16_t smem_attn[];
   uint16_t *sQ = smem_attn;
@@ -115,8 +115,9 @@ __global__ void __launch_bounds__(kPThreads, 2) attn_prefill_kernel(
   const int hk = hq / (Hq / Hkv);
   const int64_t m0 = static_cast<int64_t>(mb) * kPM;
   const uint16_t *qg = q + (static_cast<int64_t>(b) * Hq + hq) * Sq * D;
-  const uint16_t *kg = k + (static_cast<int64_t>(b) * Hkv + hk) * Skv * D;
-  const uint16_t *vg = v + (static_cast<int64_t>(b) * Hkv + hk) * Skv * D;
+  // a kv head holds kv_cap rows in memory, the first Skv of them valid
+  const uint16_t *kg = k + (static_cast<int64_t>(b) * Hkv + hk) * kv_cap * D;
+  const uint16_t *vg = v + (static_cast<int64_t>(b) * Hkv + hk) * kv_cap * D;
   const int64_t diag = Skv - Sq;  // key limit of query i is i + diag
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -280,6 +281,7 @@ constexpr int decode_smem() { return kDWarps * 2 * 2 * kDN * D * 2; }  // warps 
 struct DecodeShape {
   int Hq, Hkv, G;    // G = Hq / Hkv
   int64_t Sq, Skv;
+  int64_t kv_cap;    // rows per kv head in memory (>= Skv)
   int R;             // G * Sq rows per kv head
   int n_splits;
   int64_t split_len;
@@ -299,8 +301,8 @@ __global__ void __launch_bounds__(kDThreads) attn_decode_kernel(
   const int g = lane >> 2, t4 = lane & 3;
   const int64_t k0 = static_cast<int64_t>(split) * sh.split_len;
   const int64_t k1 = min(sh.Skv, k0 + sh.split_len);
-  const uint16_t *kg = k + (static_cast<int64_t>(b) * sh.Hkv + hk) * sh.Skv * D;
-  const uint16_t *vg = v + (static_cast<int64_t>(b) * sh.Hkv + hk) * sh.Skv * D;
+  const uint16_t *kg = k + (static_cast<int64_t>(b) * sh.Hkv + hk) * sh.kv_cap * D;
+  const uint16_t *vg = v + (static_cast<int64_t>(b) * sh.Hkv + hk) * sh.kv_cap * D;
   uint16_t *wK = smem_dec + warp * (2 * 2 * kDN * D);  // [stage][K|V][kDN][D]
 
   // Q fragments straight from global: row r -> (head hq = hk*G + r / Sq, s = r % Sq).
@@ -519,6 +521,7 @@ DecodeShape decode_shape(int64_t B, int Hq, int Hkv, int64_t Sq, int64_t Skv,
   sh.G = Hq / Hkv;
   sh.Sq = Sq;
   sh.Skv = Skv;
+  sh.kv_cap = Skv;
   sh.R = static_cast<int>(sh.G * Sq);
   const int64_t groups = B * Hkv * ((sh.R + 15) / 16);
   const int64_t want = (4LL * 148 + groups - 1) / (groups > 0 ? groups : 1);
@@ -541,14 +544,14 @@ using namespace q35;
 
 int q35_attn_prefill_tc(const void *q, const void *k, const void *v, void *out,
                         float *lse, int64_t B, int Hq, int Hkv, int64_t Sq,
-                        int64_t Skv, float scale, int causal, q35_stream_t stream);
+                        int64_t Skv, int64_t kv_cap, float scale, int causal,
+                        q35_stream_t stream);
 
-extern "C" int q35_attn_prefill_fwd(const void *q, const void *k, const void *v,
-                                    void *out, float *lse, int64_t B, int Hq,
-                                    int Hkv, int64_t Sq, int64_t Skv, int D,
-                                    float scale, int causal,
-                                    q35_stream_t stream) {
+static int attn_prefill_impl(const void *q, const void *k, const void *v, void *out, float *lse,
+                             int64_t B, int Hq, int Hkv, int64_t Sq, int64_t Skv, int64_t kv_cap,
+                             int D, float scale, int causal, q35_stream_t stream) {
   if (!q || !k || !v || !out) return fail(Q35_ERR_INVALID, "attn_prefill: null");
+  if (kv_cap < Skv) return fail(Q35_ERR_SHAPE, "attn_prefill: kv capacity below Skv");
   if (D != 32 && D != 64 && D != 128)
     return fail(Q35_ERR_UNSUPPORTED, "attn_prefill: head_dim %d (32, 64 or 128)", D);
   if (B < 0 || Sq < 0 || Skv < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0)
@@ -558,14 +561,15 @@ extern "C" int q35_attn_prefill_fwd(const void *q, const void *k, const void *v,
   if (B * Sq == 0) return Q35_OK;
   if (B * Hq > 65535) return fail(Q35_ERR_SHAPE, "attn_prefill: B*Hq > 65535");
   if (D == 128)  // tcgen05 path
-    return q35_attn_prefill_tc(q, k, v, out, lse, B, Hq, Hkv, Sq, Skv, scale, causal, stream);
+    return q35_attn_prefill_tc(q, k, v, out, lse, B, Hq, Hkv, Sq, Skv, kv_cap, scale, causal,
+                               stream);
   dim3 grid(static_cast<unsigned>((Sq + kPM - 1) / kPM), static_cast<unsigned>(B * Hq));
   auto run = [&](auto kern, int smem) -> int {
     { const int _st = ensure_smem_attr(reinterpret_cast<const void *>(kern), smem); if (_st) return _st; }
     kern<<<grid, kPThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint16_t *>(q), static_cast<const uint16_t *>(k),
         static_cast<const uint16_t *>(v), static_cast<uint16_t *>(out), lse, Hq,
-        Hkv, Sq, Skv, scale * 1.4426950408889634f, scale, causal ? 1 : 0);
+        Hkv, Sq, Skv, kv_cap, scale * 1.4426950408889634f, scale, causal ? 1 : 0);
     return Q35_OK;
   };
   int st;
@@ -577,6 +581,23 @@ extern "C" int q35_attn_prefill_fwd(const void *q, const void *k, const void *v,
   return Q35_OK;
 }
 
+extern "C" int q35_attn_prefill_fwd(const void *q, const void *k, const void *v,
+                                    void *out, float *lse, int64_t B, int Hq,
+                                    int Hkv, int64_t Sq, int64_t Skv, int D,
+                                    float scale, int causal,
+                                    q35_stream_t stream) {
+  return attn_prefill_impl(q, k, v, out, lse, B, Hq, Hkv, Sq, Skv, Skv, D, scale, causal, stream);
+}
+
+extern "C" int q35_attn_prefill_cache_fwd(const void *q, const void *k_cache,
+                                          const void *v_cache, void *out, float *lse, int64_t B,
+                                          int Hq, int Hkv, int64_t Sq, int64_t Skv,
+                                          int64_t kv_cap, int D, float scale, int causal,
+                                          q35_stream_t stream) {
+  return attn_prefill_impl(q, k_cache, v_cache, out, lse, B, Hq, Hkv, Sq, Skv, kv_cap, D, scale,
+                           causal, stream);
+}
+
 extern "C" int64_t q35_attn_decode_workspace(int64_t B, int Hq, int64_t Sq,
                                              int64_t Skv, int D) {
   if (Hq <= 0 || D <= 0) return 0;
@@ -586,12 +607,12 @@ extern "C" int64_t q35_attn_decode_workspace(int64_t B, int Hq, int64_t Sq,
          16 * (2 + static_cast<int64_t>(D)) * splits * B;
 }
 
-extern "C" int q35_attn_decode_fwd(const void *q, const void *k, const void *v,
-                                   void *out, int64_t B, int Hq, int Hkv,
-                                   int64_t Sq, int64_t Skv, int D, float scale,
-                                   float *workspace, q35_stream_t stream) {
+static int attn_decode_impl(const void *q, const void *k, const void *v, void *out, int64_t B,
+                            int Hq, int Hkv, int64_t Sq, int64_t Skv, int64_t kv_cap, int D,
+                            float scale, float *workspace, q35_stream_t stream) {
   if (!q || !k || !v || !out || !workspace)
     return fail(Q35_ERR_INVALID, "attn_decode: null pointer");
+  if (kv_cap < Skv) return fail(Q35_ERR_SHAPE, "attn_decode: kv capacity below Skv");
   if (D != 32 && D != 64 && D != 128)
     return fail(Q35_ERR_UNSUPPORTED, "attn_decode: head_dim %d (32, 64 or 128)", D);
   if (B < 0 || Sq < 1 || Skv < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0)
@@ -603,6 +624,7 @@ extern "C" int q35_attn_decode_fwd(const void *q, const void *k, const void *v,
   if (B == 0) return Q35_OK;
   if (B * Hkv > 65535) return fail(Q35_ERR_SHAPE, "attn_decode: B*Hkv > 65535");
   DecodeShape sh = decode_shape(B, Hq, Hkv, Sq, Skv, scale);
+  sh.kv_cap = kv_cap;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   dim3 grid(sh.n_splits, static_cast<unsigned>(B * Hkv), (sh.R + 15) / 16);
   const int64_t rows = B * Hkv * sh.R;
@@ -622,5 +644,57 @@ extern "C" int q35_attn_decode_fwd(const void *q, const void *k, const void *v,
   else st = run(attn_decode_kernel<32>, attn_decode_merge_kernel<32>, decode_smem<32>());
   if (st) return st;
   Q35_LAUNCH_CHECK("attn_decode merge launch");
+  return Q35_OK;
+}
+
+extern "C" int q35_attn_decode_fwd(const void *q, const void *k, const void *v,
+                                   void *out, int64_t B, int Hq, int Hkv,
+                                   int64_t Sq, int64_t Skv, int D, float scale,
+                                   float *workspace, q35_stream_t stream) {
+  return attn_decode_impl(q, k, v, out, B, Hq, Hkv, Sq, Skv, Skv, D, scale, workspace, stream);
+}
+
+extern "C" int q35_attn_decode_cache_fwd(const void *q, const void *k_cache, const void *v_cache,
+                                         void *out, int64_t B, int Hq, int Hkv, int64_t Sq,
+                                         int64_t Skv, int64_t kv_cap, int D, float scale,
+                                         float *workspace, q35_stream_t stream) {
+  return attn_decode_impl(q, k_cache, v_cache, out, B, Hq, Hkv, Sq, Skv, kv_cap, D, scale,
+                          workspace, stream);
+}
+
+// dst[b, h, offset + s, :] = src[b, h, s, :] for a [B, Hkv, cap, D] cache; one
+// warp per (b, h, s) row, 16-byte vectors.
+__global__ void __launch_bounds__(256) kv_append_kernel(const uint16_t *__restrict__ src,
+                                                         uint16_t *__restrict__ dst,
+                                                         int64_t rows, int64_t S, int64_t D,
+                                                         int64_t cap, int64_t offset) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int64_t bh = r / S, s = r - bh * S;
+  const uint4 *sp = reinterpret_cast<const uint4 *>(src + r * D);
+  uint4 *dp = reinterpret_cast<uint4 *>(dst + (bh * cap + offset + s) * D);
+  for (int64_t c = lane; c < D / 8; c += 32) dp[c] = sp[c];
+}
+
+extern "C" int q35_kv_append(const void *k_new, const void *v_new, void *k_cache, void *v_cache,
+                             int64_t B, int Hkv, int64_t S, int D, int64_t cap, int64_t offset,
+                             q35_stream_t stream) {
+  if (B < 0 || Hkv <= 0 || S < 0 || D <= 0 || D % 8 != 0 || offset < 0 || offset + S > cap)
+    return fail(Q35_ERR_SHAPE, "kv_append: offset %lld + %lld rows exceed capacity %lld",
+                (long long)offset, (long long)S, (long long)cap);
+  if (B * S == 0) return Q35_OK;  // nothing to append (empty tensors may have null pointers)
+  if (!k_new || !v_new || !k_cache || !v_cache) return fail(Q35_ERR_INVALID, "kv_append: null");
+  if (!aligned16(k_new) || !aligned16(v_new) || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(Q35_ERR_ALIGN, "kv_append: pointers not 16-byte aligned");
+  const int64_t rows = B * Hkv * S;
+  if (rows == 0) return Q35_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+  kv_append_kernel<<<grid, 256, 0, st>>>(static_cast<const uint16_t *>(k_new),
+                                         static_cast<uint16_t *>(k_cache), rows, S, D, cap, offset);
+  kv_append_kernel<<<grid, 256, 0, st>>>(static_cast<const uint16_t *>(v_new),
+                                         static_cast<uint16_t *>(v_cache), rows, S, D, cap, offset);
+  Q35_LAUNCH_CHECK("kv_append launch");
   return Q35_OK;
 }

@@ -93,6 +93,7 @@ struct AttnParams {
   float sl2;    // scale * log2(e)
   float scale;
   int causal;
+  int64_t kv_cap;  // rows per kv head in memory (>= Skv)
   uint16_t *out;
   float *lse;
   int *err;
@@ -126,7 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (p.causal) kv_end = min(p.Skv, m0 + kTile + diag);
   const int n_tiles = kv_end > 0 ? static_cast<int>((kv_end + kTile - 1) / kTile) : 0;
   const int32_t q_row = static_cast<int32_t>((static_cast<int64_t>(b) * p.Hq + h) * p.Sq + m0);
-  const int32_t kv_row = static_cast<int32_t>((static_cast<int64_t>(b) * p.Hkv + hk) * p.Skv);
+  const int32_t kv_row = static_cast<int32_t>((static_cast<int64_t>(b) * p.Hkv + hk) * p.kv_cap);
 
   if (threadIdx.x == 0) {
     sm100::mbar_init(q_full, 1);
@@ -423,7 +424,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
   int64_t kv_end = p.Skv;
   if (p.causal) kv_end = min(p.Skv, m0 + kTile + diag);
   const int n_tiles = kv_end > 0 ? static_cast<int>((kv_end + kTile - 1) / kTile) : 0;
-  const int32_t kv_row = static_cast<int32_t>((static_cast<int64_t>(b) * p.Hkv + hk) * p.Skv);
+  const int32_t kv_row = static_cast<int32_t>((static_cast<int64_t>(b) * p.Hkv + hk) * p.kv_cap);
 
   if (threadIdx.x == 0) {
     sm100::mbar_init(q_full, 1);
@@ -701,9 +702,9 @@ using namespace q35;
 // q35_attn_prefill_fwd; same arguments and layouts).
 int q35_attn_prefill_tc(const void *q, const void *k, const void *v, void *out,
                         float *lse, int64_t B, int Hq, int Hkv, int64_t Sq,
-                        int64_t Skv, float scale, int causal,
+                        int64_t Skv, int64_t kv_cap, float scale, int causal,
                         q35_stream_t stream) {
-  const int64_t qrows = B * Hq * Sq, kvrows = B * Hkv * Skv;
+  const int64_t qrows = B * Hq * Sq, kvrows = B * Hkv * kv_cap;
   if (qrows >= (int64_t(1) << 31) || kvrows >= (int64_t(1) << 31))
     return fail(Q35_ERR_SHAPE, "attn_prefill_tc: too many rows for TMA coordinates");
   int *err = device_error_word();
@@ -720,6 +721,7 @@ int q35_attn_prefill_tc(const void *q, const void *k, const void *v, void *out,
   p.Hkv = Hkv;
   p.Sq = Sq;
   p.Skv = Skv;
+  p.kv_cap = kv_cap;
   p.n_mblocks = static_cast<int>((Sq + kTile - 1) / kTile);
   p.scale = scale;
   p.sl2 = scale * 1.4426950408889634f;

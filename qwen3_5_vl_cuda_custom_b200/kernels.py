@@ -389,6 +389,49 @@ def attention_tokens(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: f
     return out
 
 
+def attention_cache(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, kv_len: int,
+                    scale: float, causal: bool) -> torch.Tensor:
+    """attention_tokens over the first ``kv_len`` rows of preallocated caches
+    k_cache/v_cache (B,Hkv,capacity,D); returns the token-major (B,Sq,Hq*D)."""
+    q = _require(q, "attention.q")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise RuntimeError("attention_cache: caches must be contiguous [B, Hkv, capacity, D]")
+    k_cache = _require(k_cache, "attention.k_cache")
+    v_cache = _require(v_cache, "attention.v_cache")
+    B, Hq, Sq, D = q.shape
+    Hkv, cap = k_cache.shape[1], k_cache.shape[2]
+    if kv_len > cap:
+        raise RuntimeError(f"attention_cache: {kv_len} rows exceed the capacity {cap}")
+    out = torch.empty(B, Sq, Hq * D, device=q.device, dtype=q.dtype)
+    with torch.cuda.device(q.device):
+        if (not causal or Sq == 1) and (Hq // Hkv) * Sq <= 16:
+            n = _lib.query("q35_attn_decode_workspace", B, Hq, Sq, kv_len, D)
+            ws = torch.empty(max(1, n), device=q.device, dtype=torch.float32)
+            _lib.call("q35_attn_decode_cache_fwd", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                      out.data_ptr(), B, Hq, Hkv, Sq, kv_len, cap, D, float(scale), ws.data_ptr(),
+                      _stream(q))
+        else:
+            _lib.call("q35_attn_prefill_cache_fwd", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                      out.data_ptr(), None, B, Hq, Hkv, Sq, kv_len, cap, D, float(scale),
+                      1 if causal else 0, _stream(q))
+    return out
+
+
+def kv_append(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+              offset: int) -> None:
+    """Writes k/v (B,Hkv,S,D) into rows [offset, offset+S) of the caches in place."""
+    k = _require(k, "kv_append.k")
+    v = _require(v, "kv_append.v")
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise RuntimeError("kv_append: caches must be contiguous")
+    _require(k_cache, "kv_append.k_cache")
+    _require(v_cache, "kv_append.v_cache")
+    B, Hkv, S, D = k.shape
+    with torch.cuda.device(k.device):
+        _lib.call("q35_kv_append", k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                  B, Hkv, S, D, k_cache.shape[2], offset, _stream(k))
+
+
 def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
                     is_causal: bool = True, num_kv_groups: int = 1) -> torch.Tensor:
     """Reference op signature (REF kernels/flash_attention.py:82-100): returns
@@ -413,5 +456,5 @@ __all__ = [
     "rmsnorm", "matmul", "softmax", "cuda_topk", "cuda_index_add", "swiglu", "residual_add",
     "router_topk", "router_split_weights", "pack_b_tiles", "moe_permute", "Permutation", "gather_rows", "grouped_gateup_swiglu",
     "grouped_down", "moe_combine", "qknorm_mrope", "mrope", "attention_tokens",
-    "flash_attention", "device_error_check", "default_scale",
+    "flash_attention", "attention_cache", "kv_append", "device_error_check", "default_scale",
 ]

@@ -12,6 +12,7 @@ import torch
 from torch import nn
 
 from .configs import MoETextConfig, Qwen3VLConfig
+from .kv_cache import KVCache
 from .modules import CudaEmbedding, CudaLinear, CudaRMSNorm, CudaTextDecoderLayer, TextMRoPE
 
 
@@ -88,3 +89,41 @@ class CudaQwen3VLMoeModel(nn.Module):
         if return_kv:
             return logits, router_logits, new_kvs
         return logits, router_logits
+
+    def make_kv_cache(self, batch: int, capacity: int, device=None) -> KVCache:
+        """A zeroed ``KVCache`` for every layer of this model (bf16)."""
+        t = self.cfg.text
+        device = device or self.embed_tokens.weight.device
+        return KVCache(len(self.layers), batch, t.num_kv_heads, capacity, t.head_dim, device)
+
+    @torch.no_grad()
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int, eos_token_id: int | None = None,
+                 kv_cache: KVCache | None = None) -> torch.Tensor:
+        """Greedy decoding: one prefill over ``input_ids`` (B, S), then one token
+        per step with the K/V history kept in a preallocated ``KVCache``
+        (capacity S + max_new_tokens unless ``kv_cache`` is given).  Returns
+        (B, S + n) token ids; stops early once every sequence has produced
+        ``eos_token_id``.  The reference generates only with its dense model
+        (REF models/dense.py:123-162); this is the same greedy loop for the MoE
+        model."""
+        B, S = input_ids.shape
+        if max_new_tokens < 1:
+            return input_ids
+        cache = kv_cache if kv_cache is not None else self.make_kv_cache(B, S + max_new_tokens,
+                                                                         input_ids.device)
+        if cache.length + S + max_new_tokens - 1 > cache[0].capacity:
+            raise RuntimeError("generate: the KV cache is too small for the requested tokens")
+        logits, _ = self.forward(input_ids, past_key_values=cache)
+        nxt = logits[:, -1].argmax(dim=-1)
+        out = [nxt]
+        done = (nxt == eos_token_id) if eos_token_id is not None else None
+        for _ in range(max_new_tokens - 1):
+            if done is not None and bool(done.all()):
+                break
+            logits, _ = self.forward(nxt[:, None], past_key_values=cache)
+            nxt = logits[:, -1].argmax(dim=-1)
+            if done is not None:
+                nxt = torch.where(done, torch.full_like(nxt, eos_token_id), nxt)
+                done = done | (nxt == eos_token_id)
+            out.append(nxt)
+        return torch.cat([input_ids, torch.stack(out, dim=1).to(input_ids.dtype)], dim=1)

@@ -23,6 +23,7 @@ import torch
 from torch import nn
 
 from . import kernels as K
+from .kv_cache import LayerKVCache
 
 
 # ------------------------------------------------------------------ norms
@@ -257,6 +258,17 @@ class CudaFullAttention(nn.Module):
         fuse its residual add and keep the post-attention residual in fp32."""
         B, S, _ = x.shape
         q, k, v = self._project(x, mrope_apply)
+        if isinstance(past_kv, LayerKVCache):
+            # preallocated cache: append in place, attend over the buffers
+            cache = past_kv
+            Sk = cache.length + S
+            if Sk > cache.capacity:
+                raise RuntimeError(f"KV cache full: {cache.length} + {S} > {cache.capacity}")
+            K.kv_append(k, v, cache.k, cache.v, cache.length)
+            causal = (S == Sk) if self.reference_chunk_mask else S > 1
+            out = K.attention_cache(q, cache.k, cache.v, Sk, self.scale, causal)
+            cache.length = Sk
+            return self.o_proj(out, residual=residual, out_dtype=out_dtype), cache
         if past_kv is not None:
             past_k, past_v = past_kv
             k = torch.cat([past_k, k], dim=2)
