@@ -7,6 +7,7 @@ mRoPE [24,20,20] theta 5e6), bf16 weights + fp32 router, prefill of
 inputs (synthetic: no checkpoint or dataset).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --workload c3   # informational: decode over a KV cache (config 3)
 
 ``value`` times the forward replayed from a CUDA graph of the module call
 (qwen3_5_vl_cuda_custom_b200.graphs.GraphedDecoderLayer); the eager module
@@ -506,6 +507,87 @@ def run_ours(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_c3(args, local):
+    """Config 3 (decode): 64 sequences x 1 new token over an 8192-position KV
+    history, one decoder layer, KV in a preallocated LayerKVCache.  Prints one
+    JSON line (decode tokens/s, HBM roofline of the step's bytes)."""
+    from qwen3_5_vl_cuda_custom_b200 import build
+    from qwen3_5_vl_cuda_custom_b200 import synthetic as syn
+    from qwen3_5_vl_cuda_custom_b200.configs import a3b_moe_text
+    from qwen3_5_vl_cuda_custom_b200.kv_cache import LayerKVCache
+    build.build()
+    dev = torch.device("cuda", local)
+    cfg = a3b_moe_text(1)
+    B, past = 64, 8192
+    layer, rot, P, g = build_layer(cfg, 2, dev)
+    cache = LayerKVCache(B, cfg.num_kv_heads, past + 1, cfg.head_dim, dev)
+    gen = torch.Generator(device=dev).manual_seed(2)
+    cache.k[:, :, :past].normal_(generator=gen)
+    cache.v[:, :, :past].normal_(generator=gen)
+    x = syn.hidden_states((B, 1, cfg.hidden_size), g).to(dev, torch.bfloat16)
+    pos = torch.full((3, B, 1), past, dtype=torch.int64, device=dev)
+    bpos = rot.bind(pos)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
+
+    def step():
+        cache.length = past  # every step appends position `past` and attends 8193 keys
+        return layer(x, bpos, past_kv=cache)
+
+    def timed(fn):
+        ms = 0.0
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ms += a.elapsed_time(b)
+        return ms / args.steps
+
+    with torch.no_grad(), ClockSampler(local) as clk:
+        clk.wait_first()
+        for _ in range(max(3, args.warmup)):
+            step()
+        eager_ms = timed(step)
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graph_ms = timed(graph.replay)
+    clocks = clk.summary()
+    ms = min(eager_ms, graph_ms)
+    peaks, peak_src = load_peaks()
+    E, k = cfg.num_experts, cfg.num_experts_per_tok
+    experts = E * (1 - (1 - 1 / E) ** (B * k))  # expected distinct experts touched
+    per_expert = 3 * cfg.moe_intermediate_size * cfg.hidden_size * 2
+    kv_bytes = 2 * B * cfg.num_kv_heads * (past + 1) * cfg.head_dim * 2
+    attn_w = (cfg.hidden_size * (cfg.num_heads + 2 * cfg.num_kv_heads) * cfg.head_dim
+              + cfg.num_heads * cfg.head_dim * cfg.hidden_size) * 2
+    hbm = kv_bytes + experts * per_expert + attn_w
+    achieved = hbm / (ms / 1e3) / 1e9
+    line = {
+        "metric": "moe_layer_decode_tokens_per_s", "value": B / (ms / 1e3), "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "C3 decode: 64 sequences x 1 token, 8192-position KV history, "
+                               "one 30B-A3B MoE decoder layer", "kv_cache": "LayerKVCache, in place",
+                   "mode": "CUDA-graph replay" if graph_ms <= eager_ms else "eager",
+                   "l2": "256 MiB flush between timed steps"},
+        "eager_ms": eager_ms, "graph_ms": graph_ms,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "algorithmic_bytes": hbm,
+                     "kv_bytes": kv_bytes, "expert_bytes": experts * per_expert,
+                     "peak_source": peak_src},
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -514,7 +596,13 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["c2", "c3"], default="c2",
+                    help="c2: the headline prefill layer (default); c3: decode over a KV cache "
+                         "(one GPU, informational line)")
     args = ap.parse_args()
+    if args.workload == "c3":
+        run_c3(args, int(os.environ.get("LOCAL_RANK", "0")))
+        return
     world, rank, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":
