@@ -499,6 +499,11 @@ def run_ours(args, world, rank, local):
                      "traffic": TRAFFIC_BYTES_C2.get(top) if S == 4096 else None,
                      "algorithmic": amount,
                      "algorithmic_bytes": ALGO_BYTES_C2.get(top) if S == 4096 else None,
+                     # the kernel's own lower bound max(FLOPs / tensor peak, bytes / HBM peak)
+                     # over its measured time (a weight-streaming GEMM can be either)
+                     "frac_of_bound": (max(amount / (peaks["bf16_tflops"] * 1e12) if bound == "tensor" else 0.0,
+                                           (ALGO_BYTES_C2.get(top) or 0.0) / (peaks["hbm_gbs"] * 1e9))
+                                       / t_top) if S == 4096 else None,
                      "peak_source": peak_src},
         "breakdown": breakdown,
         "cpu_baseline": cpu,
