@@ -24,7 +24,6 @@
 // Every mbarrier wait is bounded (sm100::mbar_wait); on timeout the kernel
 // records DEV_ERR_WAIT_TIMEOUT and unwinds.
 #include "sm100.cuh"
-#include <cstdlib>
 
 namespace q35 {
 namespace {
@@ -732,8 +731,7 @@ int q35_attn_prefill_tc(const void *q, const void *k, const void *v, void *out,
   if ((Hq / Hkv) % 2 == 0) {
     // GQA with an even group: two heads per CTA share each K/V tile.
     dim3 grid2(static_cast<unsigned>(p.n_mblocks * B * Hq / 2));
-    const char *ev = getenv("Q35_ATTN_POLY");
-    const int np = ev ? atoi(ev) : 3;
+    constexpr int np = 3;  // 3 of 8 score pairs on the FMA-pipe exp2 (measured best of 2..5)
     auto go = [&](auto kern) -> int {
       const int st2 = ensure_smem_attr(reinterpret_cast<const void *>(kern), kSmem2);
       if (st2) return st2;
@@ -751,7 +749,7 @@ int q35_attn_prefill_tc(const void *q, const void *k, const void *v, void *out,
       kern<<<grid2, kThreads2, kSmem2, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
       return 0;
     };
-    int st3 = np == 2 ? go(attn_tc2_kernel<2>) : np == 3 ? go(attn_tc2_kernel<3>) : np == 5 ? go(attn_tc2_kernel<5>) : go(attn_tc2_kernel<4>);
+    int st3 = go(attn_tc2_kernel<np>);
     if (st3) return st3;
     Q35_LAUNCH_CHECK("attn_prefill_tc2 launch");
     return Q35_OK;
