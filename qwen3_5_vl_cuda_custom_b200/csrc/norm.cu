@@ -115,6 +115,45 @@ __global__ void __launch_bounds__(256) rmsnorm_f32in_kernel(
   }
 }
 
+// cols == NV * 256 fp32 input: the whole row stays in registers (2 x NV
+// float4 per lane), all loads issued before the reduction, one pass.
+template <int NV>
+__global__ void __launch_bounds__(256) rmsnorm_f32in_reg_kernel(
+    const float *__restrict__ x, const uint16_t *__restrict__ w,
+    uint16_t *__restrict__ y, int64_t rows, float eps) {
+  constexpr int cols = NV * 256;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float *xr = x + row * cols;
+  float4 a[NV], b[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    a[i] = *reinterpret_cast<const float4 *>(xr + i * 256 + lane * 8);
+    b[i] = *reinterpret_cast<const float4 *>(xr + i * 256 + lane * 8 + 4);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    ss = fmaf(a[i].x, a[i].x, ss); ss = fmaf(a[i].y, a[i].y, ss);
+    ss = fmaf(a[i].z, a[i].z, ss); ss = fmaf(a[i].w, a[i].w, ss);
+    ss = fmaf(b[i].x, b[i].x, ss); ss = fmaf(b[i].y, b[i].y, ss);
+    ss = fmaf(b[i].z, b[i].z, ss); ss = fmaf(b[i].w, b[i].w, ss);
+  }
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(cols) + eps);
+  uint16_t *yr = y + row * cols;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    float wv[8];
+    load8(w + i * 256 + lane * 8, wv);
+    float v[8] = {a[i].x, a[i].y, a[i].z, a[i].w, b[i].x, b[i].y, b[i].z, b[i].w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = (v[j] * r) * wv[j];
+    store8(yr + i * 256 + lane * 8, v);
+  }
+}
+
 // Rotary angle table for one token: cos/sin of pos[axis(j)] * inv_freq[j] for
 // j < D/2.  axis(j) follows the reference's chunked section layout
 // (REF kernels/mrope.py:19-35: sections*2 chunks, chunk i from axis i % 3;
@@ -302,9 +341,16 @@ extern "C" int q35_rmsnorm_f32in_fwd(const float *x, const void *w, void *y,
   if (!aligned16(x) || !aligned16(w) || !aligned16(y))
     return fail(Q35_ERR_ALIGN, "rmsnorm_f32in: pointers must be 16-byte aligned");
   if (rows == 0) return Q35_OK;
-  rmsnorm_f32in_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0,
-                         reinterpret_cast<cudaStream_t>(stream)>>>(
-      x, static_cast<const uint16_t *>(w), static_cast<uint16_t *>(y), rows, cols, eps);
+  const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  auto wp = static_cast<const uint16_t *>(w);
+  auto yp = static_cast<uint16_t *>(y);
+  switch (cols) {
+    case 1024: rmsnorm_f32in_reg_kernel<4><<<grid, 256, 0, st>>>(x, wp, yp, rows, eps); break;
+    case 2048: rmsnorm_f32in_reg_kernel<8><<<grid, 256, 0, st>>>(x, wp, yp, rows, eps); break;
+    case 4096: rmsnorm_f32in_reg_kernel<16><<<grid, 256, 0, st>>>(x, wp, yp, rows, eps); break;
+    default: rmsnorm_f32in_kernel<<<grid, 256, 0, st>>>(x, wp, yp, rows, cols, eps);
+  }
   Q35_LAUNCH_CHECK("rmsnorm_f32in launch");
   return Q35_OK;
 }

@@ -36,10 +36,14 @@ def gen(seed):
 
 
 # ------------------------------------------------------------------ norms
-@pytest.mark.parametrize("rows,cols", [(4, 256), (4096, 2048), (7, 128), (3, 1000), (1, 4096)])
-def test_rmsnorm(rows, cols):
+@pytest.mark.parametrize("rows,cols", [(4, 256), (4096, 2048), (7, 128), (3, 1000), (1, 4096),
+                                       (5, 1024)])
+@pytest.mark.parametrize("fp32_in", [False, True])
+def test_rmsnorm(rows, cols, fp32_in):
+    """bf16 input, or the fp32 residual-stream input of the post-attention norm."""
     g = gen(rows * 7 + cols)
-    x = bf(torch.randn(rows, cols, generator=g))
+    x = torch.randn(rows, cols, generator=g)
+    x = x if fp32_in else bf(x)
     w = bf(1 + 0.02 * torch.randn(cols, generator=g))
     y = K().rmsnorm(x.to(DEV), w.to(DEV), 1e-6).float().cpu()
     ref = O.rmsnorm(x.float(), w.float(), 1e-6)
