@@ -736,15 +736,15 @@ int q35_attn_prefill_tc(const void *q, const void *k, const void *v, void *out,
       const int st2 = ensure_smem_attr(reinterpret_cast<const void *>(kern), kSmem2);
       if (st2) return st2;
       // the setmaxnreg split assumes exactly kRegsLaunch2 registers at launch
-      static thread_local int regs_ok[8] = {0};
-      if (!regs_ok[np & 7]) {
+      static thread_local bool regs_ok = false;
+      if (!regs_ok) {
         cudaFuncAttributes fa;
         const cudaError_t fe = cudaFuncGetAttributes(&fa, reinterpret_cast<const void *>(kern));
         if (fe != cudaSuccess) return cuda_fail(fe, "attn_prefill_tc2: cudaFuncGetAttributes");
         if (fa.numRegs != kRegsLaunch2)
           return fail(Q35_ERR_UNSUPPORTED, "attn_prefill_tc2 built with %d registers per thread, "
                       "the register split needs %d", fa.numRegs, kRegsLaunch2);
-        regs_ok[np & 7] = 1;
+        regs_ok = true;
       }
       kern<<<grid2, kThreads2, kSmem2, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
       return 0;
