@@ -350,6 +350,29 @@ Q35_API int q35_kv_append(const void *k_new, const void *v_new, void *k_cache, v
                           int64_t B, int Hkv, int64_t S, int D, int64_t cap, int64_t offset,
                           q35_stream_t stream);
 
+/* ---- Vision-tower operators (bf16, fp32 math) -------------------------- */
+/* LayerNorm over the last dim: (x - mean) * rsqrt(var + eps) * w (+ b); b may
+ * be NULL.  cols % 8 == 0.  Replaces layernorm_forward
+ * (REF kernels/layernorm.py:54, csrc/layernorm_op.cu).                       */
+Q35_API int q35_layernorm_fwd(const void *x, const void *w, const void *b, void *y,
+                              int64_t rows, int64_t cols, float eps, q35_stream_t stream);
+/* GELU, tanh approximation, elementwise over n values (n % 8 == 0).
+ * Replaces gelu_tanh_forward (REF kernels/gelu_tanh.py:49).                  */
+Q35_API int q35_gelu_tanh_fwd(const void *x, void *y, int64_t n, q35_stream_t stream);
+/* Rotate-half RoPE on the first dr of D dims of x [B,H,S,D] (the rest copied);
+ * cos/sin bf16 [B,S,dr] (per_batch != 0) or [S,dr].  D % 8 == 0, dr % 16 == 0.
+ * Replaces rope_forward (REF kernels/rope.py:58).                            */
+Q35_API int q35_rope_fwd(const void *x, const void *cos_t, const void *sin_t, void *y,
+                         int64_t B, int H, int64_t S, int D, int dr, int per_batch,
+                         q35_stream_t stream);
+/* Non-overlapping Conv3d patch embedding as a GEMM: patches bf16
+ * [n_patches, K] (each patch flattened C*T*P*P), w bf16 [embed, K], bias bf16
+ * [embed] or NULL -> out bf16 [n_patches, embed].  K % 8 == 0, embed % 32 == 0.
+ * Replaces conv3d_patch_forward (REF kernels/conv3d_patch.py:17-40).        */
+Q35_API int q35_conv3d_patch_fwd(const void *patches, const void *w, const void *bias,
+                                 void *out, int64_t n_patches, int64_t embed, int64_t K,
+                                 q35_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,6 +61,13 @@ _SIGS = {
                                           c_void_p]),
     "q35_kv_append": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_int,
                               c_int64, c_int64, c_void_p]),
+    "q35_layernorm_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float,
+                                  c_void_p]),
+    "q35_gelu_tanh_fwd": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "q35_rope_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_int,
+                             c_int, c_int, c_void_p]),
+    "q35_conv3d_patch_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                     c_void_p]),
     "q35_grouped_gemm_down": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                       c_int64, c_int, c_int, c_int, c_void_p]),
     "q35_pack_b_tiles": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p]),

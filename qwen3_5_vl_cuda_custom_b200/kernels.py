@@ -443,6 +443,64 @@ def flash_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
     return out.view(B, Sq, Hq, D).transpose(1, 2)
 
 
+# ---------------------------------------------------------------- vision ops
+def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+              eps: float = 1e-6) -> torch.Tensor:
+    """LayerNorm over the last dim, bf16 (REF kernels/layernorm.py:54)."""
+    x = _require(x, "layernorm.x")
+    weight = _require(weight.to(_BF16), "layernorm.weight")
+    bias = None if bias is None else _require(bias.to(_BF16), "layernorm.bias")
+    cols = x.shape[-1]
+    y = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        _lib.call("q35_layernorm_fwd", x.data_ptr(), weight.data_ptr(),
+                  None if bias is None else bias.data_ptr(), y.data_ptr(),
+                  x.numel() // cols if cols else 0, cols, float(eps), _stream(x))
+    return y
+
+
+def gelu_tanh(x: torch.Tensor) -> torch.Tensor:
+    """GELU with the tanh approximation, bf16 (REF kernels/gelu_tanh.py:49)."""
+    x = _require(x, "gelu_tanh.x")
+    y = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        _lib.call("q35_gelu_tanh_fwd", x.data_ptr(), y.data_ptr(), x.numel(), _stream(x))
+    return y
+
+
+def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Rotate-half RoPE on the first cos.shape[-1] dims of x (B,H,S,D); cos/sin
+    (B,S,dr) or (S,dr), cast to x's dtype as in the reference (REF
+    kernels/rope.py:58-70)."""
+    x = _require(x, "rope.x")
+    cos = _require(cos.to(x.dtype), "rope.cos")
+    sin = _require(sin.to(x.dtype), "rope.sin")
+    B, H, S, D = x.shape
+    y = torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        _lib.call("q35_rope_fwd", x.data_ptr(), cos.data_ptr(), sin.data_ptr(), y.data_ptr(),
+                  B, H, S, D, cos.shape[-1], 1 if cos.dim() == 3 else 0, _stream(x))
+    return y
+
+
+def conv3d_patch(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """Non-overlapping 3-D patch embedding (stride == kernel size): x (N, C, T, H, W)
+    with (T, H, W) the kernel size, weight (E, C, T, H, W) -> (N, E), as a GEMM of
+    the flattened patches on the tensor cores (REF kernels/conv3d_patch.py:17-40)."""
+    x = _require(x, "conv3d_patch.x")
+    w = _require(weight, "conv3d_patch.weight")
+    if tuple(x.shape[2:]) != tuple(w.shape[2:]) or x.shape[1] != w.shape[1]:
+        raise RuntimeError(f"conv3d_patch: patch {tuple(x.shape[1:])} vs kernel {tuple(w.shape[1:])}")
+    N, E = x.shape[0], w.shape[0]
+    K = x[0].numel()
+    b = None if bias is None else _require(bias.to(_BF16), "conv3d_patch.bias")
+    out = torch.empty(N, E, device=x.device, dtype=x.dtype)
+    with torch.cuda.device(x.device):
+        _lib.call("q35_conv3d_patch_fwd", x.data_ptr(), w.data_ptr(),
+                  None if b is None else b.data_ptr(), out.data_ptr(), N, E, K, _stream(x))
+    return out
+
+
 def default_scale(head_dim: int) -> float:
     return head_dim ** -0.5
 
@@ -457,4 +515,5 @@ __all__ = [
     "router_topk", "router_split_weights", "pack_b_tiles", "moe_permute", "Permutation", "gather_rows", "grouped_gateup_swiglu",
     "grouped_down", "moe_combine", "qknorm_mrope", "mrope", "attention_tokens",
     "flash_attention", "attention_cache", "kv_append", "device_error_check", "default_scale",
+    "layernorm", "gelu_tanh", "apply_rope", "conv3d_patch",
 ]
