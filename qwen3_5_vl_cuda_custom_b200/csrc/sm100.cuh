@@ -71,24 +71,6 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst,
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
-__device__ __forceinline__ void tma_load_3d(void *smem_dst,
-                                            const CUtensorMap *map,
-                                            uint64_t *bar, int32_t x,
-                                            int32_t y, int32_t z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::"
-      "bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z),
-      "r"(smem_u32(bar))
-      : "memory");
-}
-// Pulls a TMA box into L2 (no shared-memory destination, no completion).
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int32_t x, int32_t y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map))
                : "memory");
