@@ -239,6 +239,16 @@ Q35_API int q35_gemm_bf16(const void *a, const void *b, const void *bias,
                   const void *residual, void *out, int64_t M, int64_t N,
                   int64_t K, q35_stream_t stream);
 
+/* Split-K variant of q35_gemm_bf16 / q35_gemm_bf16_f32out for few rows (decode
+ * batches): k_splits fp32 partial planes are written to workspace (fp32
+ * [k_splits, M, N]) and summed in a fixed order with bias and residual;
+ * out_f32 selects an fp32 output.  K % 64 == 0 with k_splits dividing K/64.
+ * Same reference op as q35_gemm_bf16 (REF csrc/matmul_op.cpp:11-14).        */
+Q35_API int q35_gemm_bf16_splitk(const void *a, const void *b, const void *bias,
+                                 const void *residual, void *out, int out_f32, int64_t M,
+                                 int64_t N, int64_t K, int k_splits, float *workspace,
+                                 q35_stream_t stream);
+
 /* Same GEMM with an fp32 output: out[m,n] = acc + bias[n] + residual[m,n]
  * stored as fp32 (residual bf16).  The decoder layer uses it for o_proj so the
  * post-attention residual h = x + attn is rounded once, at the layer output

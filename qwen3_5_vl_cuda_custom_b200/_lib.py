@@ -68,6 +68,8 @@ _SIGS = {
                              c_int, c_int, c_void_p]),
     "q35_conv3d_patch_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                      c_void_p]),
+    "q35_gemm_bf16_splitk": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int64,
+                                     c_int64, c_int64, c_int, c_void_p, c_void_p]),
     "q35_grouped_gemm_down": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                       c_int64, c_int, c_int, c_int, c_void_p]),
     "q35_pack_b_tiles": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p]),

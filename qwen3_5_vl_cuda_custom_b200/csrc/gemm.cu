@@ -940,6 +940,91 @@ static int gemm_dense(const void *a, const void *b, const void *bias,
   return launch_gemm<128, EPI_PLAIN, 6>(ta, tb, p, tiles, s);
 }
 
+// out[m, n] = sum_s ws[s, m, n] (fixed order) + bias[n] + residual[m, n]; bf16
+// or fp32 output.  Thread = 4 consecutive outputs.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(
+    const float *__restrict__ ws, int splits, int64_t plane, const uint16_t *__restrict__ bias,
+    const uint16_t *__restrict__ residual, void *__restrict__ out, int out_f32, int64_t N) {
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (i >= plane) return;
+  float4 acc = *reinterpret_cast<const float4 *>(ws + i);
+  for (int s = 1; s < splits; ++s) {
+    const float4 v = *reinterpret_cast<const float4 *>(ws + s * plane + i);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  float r[4] = {acc.x, acc.y, acc.z, acc.w};
+  if (bias) {
+    const int64_t n = i % N;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r[j] += bf2f(bias[n + j]);
+  }
+  if (residual) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r[j] = bf2f(residual[i + j]) + r[j];
+  }
+  if (out_f32) {
+    *reinterpret_cast<float4 *>(static_cast<float *>(out) + i) = make_float4(r[0], r[1], r[2], r[3]);
+  } else {
+    uint2 u;
+    u.x = pack_bf2(r[0], r[1]);
+    u.y = pack_bf2(r[2], r[3]);
+    *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(out) + i) = u;
+  }
+}
+
+// Split-K dense GEMM for few rows (decode-sized M): the 1-CTA tcgen05 kernel
+// writes k_splits fp32 partial planes [k_splits, M, N] into `workspace`, so
+// ceil(N/128) * k_splits CTAs share the weight stream instead of ceil(N/128);
+// the reduce kernel adds them in a fixed order with bias and residual.
+extern "C" int q35_gemm_bf16_splitk(const void *a, const void *b, const void *bias,
+                                    const void *residual, void *out, int out_f32, int64_t M,
+                                    int64_t N, int64_t K, int k_splits, float *workspace,
+                                    q35_stream_t stream) {
+  if (!a || !b || !out || !workspace) return fail(Q35_ERR_INVALID, "gemm_splitk: null pointer");
+  if (M < 0 || N <= 0 || K <= 0 || N % 32 != 0 || K % kBK != 0 || k_splits < 1 ||
+      (K / kBK) % k_splits != 0)
+    return fail(Q35_ERR_SHAPE, "gemm_splitk: K %lld must be x64 with %d splits dividing its "
+                "k-blocks, N %lld x32", (long long)K, k_splits, (long long)N);
+  if (M >= (int64_t(1) << 31) || N >= (int64_t(1) << 24))
+    return fail(Q35_ERR_SHAPE, "gemm_splitk: M/N too large");
+  if (!aligned16(out) || !aligned16(workspace) || (residual && !aligned16(residual)) ||
+      (bias && !aligned16(bias)))
+    return fail(Q35_ERR_ALIGN, "gemm_splitk: pointers not 16-byte aligned");
+  if (M == 0) return Q35_OK;
+  int *err = device_error_word();
+  if (!err) return fail(Q35_ERR_CUDA, "gemm_splitk: no device error word");
+  CUtensorMap ta, tb;
+  int st = make_tmap_bf16_2d(&ta, a, K, M, K * 2, kBK, kBM);
+  if (st) return st;
+  st = make_tmap_bf16_2d(&tb, b, K, N, K * 2, kBK, 64);
+  if (st) return st;
+  GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.E = 1;
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.n_tiles = static_cast<int>((N + 127) / 128);
+  p.b_rows_per_group = static_cast<int>(N);
+  p.b_tile_step = 128;
+  p.b_second_off = 64;
+  p.out = reinterpret_cast<uint16_t *>(workspace);
+  p.ldo = N;
+  p.err = err;
+  p.out_f32 = 1;
+  p.k_splits = k_splits;
+  p.split_stride = M * N;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int tiles = static_cast<int>(((M + kBM - 1) / kBM) * p.n_tiles * k_splits);
+  st = launch_gemm<128, EPI_PLAIN, 6>(ta, tb, p, tiles, s);
+  if (st) return st;
+  const int64_t plane = M * N;
+  splitk_reduce_kernel<<<static_cast<unsigned>((plane / 4 + 255) / 256), 256, 0, s>>>(
+      workspace, k_splits, plane, static_cast<const uint16_t *>(bias),
+      static_cast<const uint16_t *>(residual), out, out_f32 ? 1 : 0, N);
+  Q35_LAUNCH_CHECK("gemm_splitk reduce launch");
+  return Q35_OK;
+}
+
 extern "C" int q35_gemm_bf16(const void *a, const void *b, const void *bias,
                              const void *residual, void *out, int64_t M,
                              int64_t N, int64_t K, q35_stream_t stream) {

@@ -82,11 +82,40 @@ def matmul(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
         residual = _require(residual, "matmul.residual")
         if residual.shape != out.shape:
             raise RuntimeError("matmul: residual shape must equal the output shape")
+    splits = _splitk_factor(M, N, K, x.device)
     with torch.cuda.device(x.device):
-        _lib.call("q35_gemm_bf16" if out_dtype == _BF16 else "q35_gemm_bf16_f32out",
-                  x.data_ptr(), weight.data_ptr(), _ptr(bias), _ptr(residual),
-                  out.data_ptr(), M, N, K, _stream(x))
+        if splits > 1:
+            # few rows: split K so more SMs share the weight stream
+            ws = torch.empty(splits * M * N, device=x.device, dtype=torch.float32)
+            _lib.call("q35_gemm_bf16_splitk", x.data_ptr(), weight.data_ptr(), _ptr(bias),
+                      _ptr(residual), out.data_ptr(), 1 if out_dtype == torch.float32 else 0,
+                      M, N, K, splits, ws.data_ptr(), _stream(x))
+        else:
+            _lib.call("q35_gemm_bf16" if out_dtype == _BF16 else "q35_gemm_bf16_f32out",
+                      x.data_ptr(), weight.data_ptr(), _ptr(bias), _ptr(residual),
+                      out.data_ptr(), M, N, K, _stream(x))
     return out
+
+
+_SM_COUNT: dict[int, int] = {}
+
+
+def _splitk_factor(M: int, N: int, K: int, device) -> int:
+    """K splits for a dense GEMM of at most 128 rows: the largest power of two
+    (<= 16) that divides the 64-wide k-blocks and keeps ceil(N/128) * splits
+    CTAs within one wave; 1 (no split) for larger M or when it would not help."""
+    if M == 0 or M > 128 or K % 64 != 0 or N % 32 != 0:
+        return 1
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    sms = _SM_COUNT.get(idx)
+    if sms is None:
+        sms = _SM_COUNT[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    tiles = -(-N // 128)
+    splits = 1
+    for s in (2, 4, 8, 16):
+        if (K // 64) % s == 0 and tiles * s <= sms:
+            splits = s
+    return splits if tiles * 2 <= sms else 1
 
 
 # ---------------------------------------------------------------- routing

@@ -52,8 +52,27 @@ def test_rmsnorm(rows, cols, fp32_in):
 
 
 # ------------------------------------------------------------------ GEMM
+@pytest.mark.parametrize("M", [64, 17])
+def test_gemm_splitk_with_residual_and_fp32_out(M):
+    """Decode-sized rows take the split-K path: partial planes summed with the
+    bias and the bf16 residual, fp32 or bf16 output."""
+    g = gen(M)
+    N, K_ = 2048, 4096
+    a = bf(torch.randn(M, K_, generator=g))
+    b = bf(torch.randn(N, K_, generator=g) * 0.02)
+    bias = bf(torch.randn(N, generator=g) * 0.1)
+    res = bf(torch.randn(M, N, generator=g))
+    Kk = K()
+    assert Kk._splitk_factor(M, N, K_, torch.device(DEV)) > 1
+    ref = a.float() @ b.float().t() + bias.float() + res.float()
+    for dt in (torch.float32, torch.bfloat16):
+        out = Kk.matmul(a.to(DEV), b.to(DEV), bias.to(DEV), residual=res.to(DEV), out_dtype=dt)
+        err = (out.float().cpu() - ref).abs().max()
+        assert err <= 1e-2 * ref.abs().max() + 1e-3, float(err)
+
 @pytest.mark.parametrize("M,N,K_", [(8, 64, 64), (128, 128, 64), (300, 384, 256), (4096, 5120, 2048),
-                                    (4096, 2048, 4096), (1, 256, 128), (129, 2048, 768)])
+                                    (4096, 2048, 4096), (1, 256, 128), (129, 2048, 768),
+                                    (64, 5120, 2048), (64, 2048, 4096), (3, 96, 640)])
 def test_gemm(M, N, K_):
     g = gen(M + N + K_)
     a = bf(torch.randn(M, K_, generator=g))
