@@ -1,28 +1,39 @@
 """Benchmark: Qwen3-VL-MoE decoder-layer prefill tokens/s on B200.
 
-Workload: one 30B-A3B-shaped MoE decoder layer
-(hidden 2048, 32/4 heads x 128, QK-norm, 128 experts top-8, intermediate 768,
-mRoPE [24,20,20] theta 5e6), bf16 weights + fp32 router, prefill of
-1 x 4096 tokens per GPU, causal, seed 1, random-init weights and N(0,1)
-inputs (synthetic: no checkpoint or dataset).
+Workloads (synthetic seeded inputs, random-init weights
+of the 30B-A3B layer shape -- no checkpoint or dataset exists here):
+
+  c2 (default, configs[1]): one MoE decoder layer (hidden 2048, 32/4 heads x
+     128, QK-norm, 128 experts top-8, intermediate 768, mRoPE [24,20,20]
+     theta 5e6), bf16 weights + fp32 router, prefill of 1 x 4096 tokens PER
+     GPU, causal, seed 1.  N > 1: every rank prefills its own sequence and the
+     experts are sharded expert-parallel (128/N per GPU); "scaling": "weak".
+  c4: the global batch of 8 x 2048 tokens split over the N
+     ranks (8/N sequences each; "scaling": "strong"), token ids uniform over
+     the 151936-entry vocabulary gathered from an N(0, 0.02) embedding table
+     before the timed region, router logits skewed by 0.5*log Zipf(1.2)
+     popularity, seed 3.  One layer per step (the 48 layers of the stack have
+     identical shapes; the stack time is 48 x the layer time plus nothing
+     else on this path).
+  c5: 4 x 2048 tokens per GPU with a 16x16 image grid at offset
+     64 (multimodal mRoPE positions), seed 4, "weak".
+  c3 (configs[2], one GPU, informational): decode of 64 sequences x 1 token
+     over an 8192-position KV history.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-  python bench.py --workload c3   # informational: decode over a KV cache (config 3)
+                  [--workload c2|c3|c4|c5]
 
 ``value`` times the forward replayed from a CUDA graph of the module call
 (qwen3_5_vl_cuda_custom_b200.graphs.GraphedDecoderLayer); the eager module
-call is reported beside it.
-
-One process per GPU (torchrun for N > 1).  Each rank prefills its own
-4096-token sequence (attention data-parallel over sequences) and the experts
-are sharded expert-parallel, 128/N per GPU, with NCCL all-to-all dispatch and
-return (qwen3_5_vl_cuda_custom_b200.ep); per-GPU work is fixed ("scaling":
-"weak").
-A step is one layer forward; the L2 is flushed (256 MiB write) between
-steps outside the timed events.  ``value`` is whole-job tokens/s from
-per-step CUDA events (max over ranks); ``e2e`` re-times the same step through
-the public module API with the input copied from pinned host memory and the
-output copied back inside the timed region.
+call is reported beside it.  The L2 is flushed (256 MiB write) between steps
+outside the timed events.  ``value`` is whole-job tokens/s from per-step CUDA
+events (max over ranks); ``e2e`` re-times the same step through the public
+module API with the input copied from pinned host memory and the output
+copied back inside the timed region.  ``breakdown`` holds device-only stage
+times: each stage of the layer is captured in its own CUDA graph and replayed
+after an L2 flush (median of 7).  At N > 1 a ``parity`` object checks the
+expert-parallel layer of every rank against the CPU oracle (outside the timed
+region).
 """
 from __future__ import annotations
 
@@ -41,13 +52,16 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-# DRAM bytes (read + write) per launch from `ncu --set full` captures of the C2
-# workload (profiles/grouped_gemm_pair_c2_full.md, profiles/attention_tc2_c2_full.md)
+# DRAM bytes (read + write) per launch from single-kernel ncu captures of the
+# C2 workload, and the algorithmic bytes of the same launches (weights + rows
+# read, outputs written).  Only C2 has captures.
 TRAFFIC_BYTES_C2 = {"gate_up_swiglu": 1055.5e6, "down": 575.9e6, "attention": 42.9e6}
-# algorithmic bytes of the same launches (weights + rows read, outputs written)
 ALGO_BYTES_C2 = {"gate_up_swiglu": 989.8e6, "down": 587.2e6, "attention": 75.5e6}
-LINK_GBS = 770.0  # measured NVLink peer copy per direction on this pool
+# NVLink peer copy per direction measured on this pool's B200s (used only when
+# the run cannot measure its own figure, i.e. at N = 1)
+LINK_GBS_POOL = 770.0
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC = "moe_layer_prefill_tokens_per_s"
 
 
 def load_peaks() -> tuple[dict, str]:
@@ -118,21 +132,91 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-# ---------------------------------------------------------------- workload
-def build_layer(cfg, seed: int, device, expert_group=None):
+# ---------------------------------------------------------------- workloads
+class Workload:
+    """Seeded inputs of one configuration for one rank.
+
+    Fields: cfg, P (fp32 CPU state dict of the layer, bf16-rounded), bias
+    (router bias or None), x_cpu (this rank's (B, S, H) fp32 input, values
+    exact in bf16), pos_cpu ((3, B, S) int64), name, scaling, tokens_global."""
+
+
+def make_workload(name: str, world: int, rank: int, tokens: int | None = None) -> Workload:
     from qwen3_5_vl_cuda_custom_b200 import synthetic as syn
+    from qwen3_5_vl_cuda_custom_b200.configs import a3b_moe_text
+    w = Workload()
+    w.name = name
+    w.cfg = cfg = a3b_moe_text(1)
+    H = cfg.hidden_size
+    w.bias = None
+    if name == "c2":
+        S = tokens or 4096
+        g = torch.Generator().manual_seed(1)
+        w.P = syn.layer_params(cfg, g)
+        if rank > 0:  # every rank prefills its own sequence
+            g = torch.Generator().manual_seed(1000 + rank)
+        w.x_cpu = syn.hidden_states((1, S, H), g)
+        w.pos_cpu = syn.text_positions(1, S)
+        w.scaling, w.tokens_global = "weak", world * S
+        w.desc = f"C2 30B-A3B MoE decoder layer prefill, 1x{S} tokens per GPU"
+    elif name == "c4":
+        B, S = 8, tokens or 2048
+        if B % world:
+            raise SystemExit(f"c4: 8 sequences do not split over {world} ranks")
+        Bl = B // world
+        g = torch.Generator().manual_seed(3)
+        w.P = syn.layer_params(cfg, g)
+        w.bias = syn.zipf_router_bias(cfg.num_experts, g)
+        ids = torch.randint(0, cfg.vocab_size, (B, S), generator=g)
+        w.ids = ids[rank * Bl:(rank + 1) * Bl]
+        w.x_cpu = None  # gathered from the embedding table on the GPU
+        w.pos_cpu = syn.text_positions(Bl, S)
+        w.scaling, w.tokens_global = "strong", B * S
+        w.desc = (f"C4 30B-A3B MoE decoder layer prefill, global batch {B}x{S} split over "
+                  f"{world} GPU(s), Zipf(1.2) router skew")
+    elif name == "c5":
+        B, S = 4, tokens or 2048
+        g = torch.Generator().manual_seed(4)
+        w.P = syn.layer_params(cfg, g)
+        if rank > 0:
+            g = torch.Generator().manual_seed(4000 + rank)
+        w.x_cpu = syn.multimodal_hidden(B, S, H, g)
+        w.pos_cpu = syn.multimodal_positions(B, S)
+        w.scaling, w.tokens_global = "weak", world * B * S
+        w.desc = f"C5 30B-A3B MoE decoder layer prefill, {B}x{S} multimodal tokens per GPU"
+    else:
+        raise SystemExit(f"unknown workload {name}")
+    return w
+
+
+def c4_embedding_input(w: Workload, dev) -> torch.Tensor:
+    """C4 hidden inputs: rows of an N(0, 0.02) bf16 embedding table (drawn on the
+    GPU from seed 3) gathered by the token ids, through CudaEmbedding."""
+    from qwen3_5_vl_cuda_custom_b200.modules import CudaEmbedding
+    cfg = w.cfg
+    emb = CudaEmbedding(cfg.vocab_size, cfg.hidden_size).to(dev, torch.bfloat16)
+    gd = torch.Generator(device=dev).manual_seed(3)
+    with torch.no_grad():
+        emb.weight.normal_(0.0, 0.02, generator=gd)
+        x = emb(w.ids.to(dev))
+    del emb
+    return x
+
+
+def build_layer(w: Workload, device, expert_group=None):
     from qwen3_5_vl_cuda_custom_b200.modules import CudaTextDecoderLayer, TextMRoPE
-    g = torch.Generator().manual_seed(seed)
-    P = syn.layer_params(cfg, g)
+    cfg = w.cfg
     layer = CudaTextDecoderLayer(cfg.hidden_size, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
                                  cfg.intermediate_size, cfg.rms_norm_eps, use_moe=True,
                                  num_experts=cfg.num_experts, top_k=cfg.num_experts_per_tok,
                                  moe_intermediate_size=cfg.moe_intermediate_size,
                                  expert_group=expert_group)
-    layer.load_state_dict(P)  # expert-parallel layers keep their slice of the experts
+    layer.load_state_dict(w.P)  # expert-parallel layers keep their slice of the experts
     layer = layer.to(device, torch.bfloat16)
+    if w.bias is not None:
+        layer.mlp.router_bias = w.bias.to(device, torch.float32)
     rot = TextMRoPE(cfg.head_dim, cfg.rope_theta, cfg.mrope_section).to(device)
-    return layer, rot, P, g
+    return layer, rot
 
 
 def stage_table(cfg, T: int, S: int, world: int = 1) -> dict:
@@ -147,103 +231,155 @@ def stage_table(cfg, T: int, S: int, world: int = 1) -> dict:
         "qkv_norm_rope": ("tensor", 2 * T * H * (Hq + 2 * Hkv) * D),
         "attention": ("tensor", B * Hq * 4 * D * S * (S + 1) / 2),
         "o_proj_residual": ("tensor", 2 * T * Hq * D * H),
-        "post_rmsnorm": ("hbm", 2 * T * H * 2),
+        # fp32 residual stream in, bf16 out
+        "post_rmsnorm": ("hbm", T * H * 4 + T * H * 2),
         "router": ("hbm", T * H * 2 + T * E * 4 + T * k * 8),
         "permute": ("hbm", T * k * 4 * 3),
         "gather": ("hbm", T * H * 2 + T * k * H * 2),
         "gate_up_swiglu": ("tensor", T * k * 2 * H * 2 * I),
         "down": ("tensor", T * k * 2 * I * H),
-        "combine_residual": ("hbm", T * k * H * 2 + 2 * T * H * 2 + T * k * 4),
-        # expert parallelism: one row per (token, destination rank), each
-        # direction; expected ranks per token N(1 - (1 - 1/N)^k), N = world
-        "ep_dispatch": ("link", T * H * 2 * world * (1 - (1 - 1 / world) ** k)),
-        "experts_chunk0": ("tensor", T * k * 2 * 3 * H * I / 2),
-        "ep_return": ("link", T * H * 2 * world * (1 - (1 - 1 / world) ** k)),
+        # k bf16 slot rows + fp32 residual read, bf16 out, weights
+        "combine_residual": ("hbm", T * k * H * 2 + T * H * 4 + T * H * 2 + T * k * 4),
+        # expert parallel: dispatch + experts + return + combine in one stage
+        "moe_expert_parallel": ("tensor", T * k * 2 * 3 * H * I),
     }
 
 
-def staged_forward(layer, rot, x, pos, marks=None):
-    """The decoder-layer forward (the same kernel sequence as the module path),
-    with an optional CUDA event recorded after each stage."""
+def layer_stages(layer, rot, x, pos):
+    """The decoder-layer forward as a list of (name, fn(state)) stages -- the
+    same kernel sequence as CudaTextDecoderLayer.forward, split so that each
+    stage can be captured and timed on its own."""
     from qwen3_5_vl_cuda_custom_b200 import kernels as K
     att, moe = layer.self_attn, layer.mlp
     B, S, H = x.shape
+    st = {"x": x}
+    stages = []
 
-    def mark(name):
-        if marks is not None:
-            ev = torch.cuda.Event(enable_timing=True)
-            ev.record()
-            marks.append((name, ev))
+    def add(name):
+        def deco(fn):
+            stages.append((name, fn))
+            return fn
+        return deco
 
-    mark("start")
-    xn = K.rmsnorm(x, layer.input_layernorm.weight, layer.input_layernorm.eps)
-    mark("input_rmsnorm")
-    w, _ = att._qkv_weight()
-    if att.fuse_qkv_epilogue and att.head_dim == 128 and B * S >= 256:
-        q, k, v = K.qkv_proj_norm_rope(xn, w, att.q_norm.weight, att.k_norm.weight, pos,
-                                       rot.inv_freq, rot.mrope_section, att.num_heads,
-                                       att.num_kv_heads, att.q_norm.eps)
-        mark("qkv_norm_rope")
-    else:
-        qkv = K.matmul(xn, w)
-        mark("qkv_gemm")
-        q, k, v = K.qknorm_mrope(qkv, att.q_norm.weight, att.k_norm.weight, pos, rot.inv_freq,
-                                 rot.mrope_section, B, S, att.num_heads, att.num_kv_heads,
-                                 att.head_dim, att.q_norm.eps)
-        mark("qknorm_mrope")
-    o = K.attention_tokens(q, k, v, att.scale, True)
-    mark("attention")
-    h = K.matmul(o, att.o_proj.weight, residual=x, out_dtype=torch.float32)
-    mark("o_proj_residual")
-    m_in = K.rmsnorm(h, layer.post_attention_layernorm.weight, layer.post_attention_layernorm.eps)
-    mark("post_rmsnorm")
-    m2 = m_in.reshape(-1, H)
-    logits, idx, wts = moe.route(m2)
-    mark("router")
-    if getattr(moe, "exchange", None) is not None:  # expert parallel
-        out = moe.experts(m2, idx, wts, h.reshape(-1, H), mark=mark)
-        mark("combine_residual")
-        return out.reshape(B, S, H)
-    perm = K.moe_permute(idx, moe.num_experts)
-    mark("permute")
-    xs = K.gather_rows(m2, perm.sorted_tok)
-    mark("gather")
-    gu_p, dn_p = moe._packed_experts()
-    act = K.grouped_gateup_swiglu(xs, moe.gate_up_proj, perm, w_packed=gu_p)
-    mark("gate_up_swiglu")
-    y = K.grouped_down(act, moe.down_proj, perm, w_packed=dn_p)
-    mark("down")
-    out = K.moe_combine(y, wts, perm.slot_pos, h.reshape(-1, H), B * S, H)
-    mark("combine_residual")
-    return out.reshape(B, S, H)
+    @add("input_rmsnorm")
+    def _(st):
+        st["xn"] = K.rmsnorm(st["x"], layer.input_layernorm.weight, layer.input_layernorm.eps)
+
+    @add("qkv_norm_rope")
+    def _(st):
+        w, _b = att._qkv_weight()
+        st["q"], st["k"], st["v"] = K.qkv_proj_norm_rope(
+            st["xn"], w, att.q_norm.weight, att.k_norm.weight, pos, rot.inv_freq,
+            rot.mrope_section, att.num_heads, att.num_kv_heads, att.q_norm.eps)
+
+    @add("attention")
+    def _(st):
+        st["o"] = K.attention_tokens(st["q"], st["k"], st["v"], att.scale, True)
+
+    @add("o_proj_residual")
+    def _(st):
+        st["h"] = K.matmul(st["o"], att.o_proj.weight, residual=st["x"], out_dtype=torch.float32)
+
+    @add("post_rmsnorm")
+    def _(st):
+        st["m2"] = K.rmsnorm(st["h"], layer.post_attention_layernorm.weight,
+                             layer.post_attention_layernorm.eps).reshape(-1, H)
+
+    @add("router")
+    def _(st):
+        st["logits"], st["idx"], st["wts"] = moe.route(st["m2"])
+
+    if getattr(moe, "exchange", None) is not None:
+        @add("moe_expert_parallel")
+        def _(st):
+            st["out"] = moe.experts(st["m2"], st["idx"], st["wts"], st["h"].reshape(-1, H))
+        return stages, st
+
+    @add("permute")
+    def _(st):
+        st["perm"] = K.moe_permute(st["idx"], moe.num_experts)
+
+    @add("gather")
+    def _(st):
+        st["xs"] = K.gather_rows(st["m2"], st["perm"].sorted_tok)
+
+    @add("gate_up_swiglu")
+    def _(st):
+        st["act"] = K.grouped_gateup_swiglu(st["xs"], moe.gate_up_proj, st["perm"])
+
+    @add("down")
+    def _(st):
+        st["y"] = K.grouped_down(st["act"], moe.down_proj, st["perm"])
+
+    @add("combine_residual")
+    def _(st):
+        st["out"] = K.moe_combine(st["y"], st["wts"], st["perm"].slot_pos,
+                                  st["h"].reshape(-1, H), B * S, H)
+    return stages, st
 
 
-LAUNCHES_PER_LAYER = 16  # rmsnorm, rope table, qkv+norm+rope, attn, o, rmsnorm, router logits,
-# router top-k, permute x3 (count, scan, scatter), gather, gate_up, down, combine
+def stage_breakdown(layer, rot, x, pos, flush, world, reps: int = 7) -> dict:
+    """Device-only time of every stage: each stage is captured in its own CUDA
+    graph (inputs from the previous stage's captured outputs) and replayed
+    after an L2 flush; median of ``reps`` replays, max over ranks."""
+    stages, st = layer_stages(layer, rot, x, pos)
+    for _, fn in stages:  # eager pass: fills the state and the weight caches
+        fn(st)
+    torch.cuda.synchronize()
+    graphs = []
+    for name, fn in stages:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn(st)
+        graphs.append((name, g))
+    barrier(world)
+    out = {}
+    for name, g in graphs:
+        g.replay()
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            ts.append((a, b))
+        torch.cuda.synchronize()
+        out[name] = allreduce_max(statistics.median(a.elapsed_time(b) for a, b in ts), world)
+    del graphs
+    return out
 
 
-def cpu_reference_step_fn(cfg, P, x_cpu, pos_cpu, dtype):
-    """The reference's own CudaTextDecoderLayer (baseline/_ref) on CPU tensors,
-    or None when the reference is not installed."""
+def cpu_reference_layer(w: Workload, dtype, sample_tokens: int):
+    """The reference's own CudaTextDecoderLayer (baseline/_ref) on CPU tensors
+    over the first ``sample_tokens`` tokens of the first sequence, or None when
+    the reference is not installed.  Returns (step, tokens per step).  The
+    reference has no router-bias hook; the bias only moves which experts
+    run, not how much work the layer does (top-k rows per token are fixed)."""
     ref_dir = ROOT / "baseline" / "_ref"
     if not (ref_dir / "cuda_qwen3_vl").exists():
-        return None
+        return None, 0
     os.environ.setdefault("CUDA_QWEN3_VL_AUTO_PRELOAD", "0")
     sys.path.insert(0, str(ref_dir))
     from cuda_qwen3_vl.modules import CudaTextDecoderLayer, TextMRoPE
+    cfg = w.cfg
     layer = CudaTextDecoderLayer(cfg.hidden_size, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
                                  cfg.intermediate_size, cfg.rms_norm_eps, use_moe=True,
                                  num_experts=cfg.num_experts, top_k=cfg.num_experts_per_tok,
                                  moe_intermediate_size=cfg.moe_intermediate_size)
-    layer.load_state_dict(P)
+    layer.load_state_dict(w.P)
     layer = layer.to(dtype)
     rot = TextMRoPE(cfg.head_dim, theta=cfg.rope_theta, mrope_section=cfg.mrope_section)
-    xr = x_cpu.to(dtype)
+    x = w.x_cpu if w.x_cpu is not None else torch.randn(w.pos_cpu.shape[1:] + (cfg.hidden_size,),
+                                                        generator=torch.Generator().manual_seed(3))
+    n = min(sample_tokens, x.shape[1])
+    xr = x[:1, :n].to(dtype).contiguous()
+    pos = w.pos_cpu[:, :1, :n].contiguous()
 
     def step():
         with torch.no_grad():
-            return layer(xr, lambda q, k: rot.apply(q, k, pos_cpu))[0]
-    return step
+            return layer(xr, lambda q, k: rot.apply(q, k, pos))[0]
+    return step, n
 
 
 def time_cpu(step, warmup: int, steps: int) -> list[float]:
@@ -255,6 +391,35 @@ def time_cpu(step, warmup: int, steps: int) -> list[float]:
         step()
         ts.append(time.perf_counter() - t0)
     return ts
+
+
+def cpu_baseline(w: Workload, steps: int = 3) -> dict:
+    """The reference's CPU path on the host cores: bf16 (the GPU's dtype; the
+    reported value) and fp32, each the median of ``steps`` calls after one
+    warm-up, on a bounded sample of the workload (one sequence)."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sample = 4096 if w.name == "c2" else 2048
+    out = {"unit": "tokens/s", "cores": threads}
+    for dtype, key in ((torch.bfloat16, "value"), (torch.float32, "fp32_value")):
+        step, n = cpu_reference_layer(w, dtype, sample)
+        kind = "reference"
+        if step is None:  # the oracle port of the same path
+            from oracle import layer_oracle as O
+            kind = "port"
+            n = min(sample, w.pos_cpu.shape[2])
+            xs = (w.x_cpu if w.x_cpu is not None else
+                  torch.randn(1, n, w.cfg.hidden_size))[:1, :n]
+            pos = w.pos_cpu[:, :1, :n]
+
+            def step():
+                return O.decoder_layer(xs, w.P, w.cfg, pos, router_bias=w.bias)["out"]
+        ts = time_cpu(step, 1, steps)
+        out[key] = n / statistics.median(ts)
+        out["kind"] = kind
+        out.setdefault("sample", f"one layer over {n} tokens of one sequence, median of {steps} "
+                                 f"after 1 warm-up, bf16 (fp32_value: same in fp32)")
+    return out
 
 
 def dist_setup(n_gpus: int):
@@ -289,74 +454,127 @@ def barrier(world: int):
     torch.cuda.synchronize()
 
 
+def measure_link(world: int, rank: int, dev, nbytes: int = 256 << 20) -> float | None:
+    """Peer bandwidth per direction: ranks (2i, 2i+1) exchange ``nbytes`` with
+    NCCL send/recv at the same time; GB/s of the slowest rank (median of 5)."""
+    if world < 2:
+        return None
+    import torch.distributed as dist
+    peer = rank ^ 1
+    if peer >= world:
+        return None
+    a = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    b = torch.empty_like(a)
+    ts = []
+    for i in range(7):
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ops = [dist.P2POp(dist.isend, a, peer), dist.P2POp(dist.irecv, b, peer)]
+        for r in dist.batch_isend_irecv(ops):
+            r.wait()
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= 2:
+            ts.append(e0.elapsed_time(e1))
+    ms = allreduce_max(statistics.median(ts), world)
+    return nbytes / (ms / 1e3) / 1e9
+
+
+def ep_parity(layer, rot, w: Workload, x, pos, world: int, n_tokens: int = 512) -> dict:
+    """Expert-parallel layer output of this rank vs the CPU oracle on the first
+    ``n_tokens`` tokens of its first sequence.  The oracle re-runs with the
+    GPU's expert choice (the top-k choice is a discrete function of the bf16
+    MoE input), and the router ids on the GPU's own MoE input must match the
+    oracle's outside near ties.  All ranks call the layer together (the
+    exchange is collective); the result is reduced over ranks."""
+    from oracle import layer_oracle as O
+    cfg, H = w.cfg, w.cfg.hidden_size
+    n = min(n_tokens, x.shape[1])
+    xs = x[:1, :n].contiguous()
+    ps = pos[:, :1, :n].contiguous()
+    with torch.no_grad():
+        y, _, _ = layer(xs, rot.bind(ps))
+        h = layer.self_attn(layer.input_layernorm(xs), rot.bind(ps), residual=xs,
+                            out_dtype=torch.float32)[0]
+        m_in = layer.post_attention_layernorm(h).reshape(-1, H)
+        logits, idx, _ = layer.mlp.route(m_in)
+    torch.cuda.synchronize()
+    xc = xs.float().cpu()
+    bias = None if w.bias is None else w.bias
+    ref = O.decoder_layer(xc, w.P, cfg, ps.cpu(), router_bias=bias, force_idx=idx.cpu())
+    st = O.error_stats(y.float().cpu(), ref["out"])
+    _, p, ridx, _ = O.router(m_in.float().cpu(), w.P["mlp.gate_weight"], cfg.num_experts_per_tok,
+                             True, bias)
+    ok_rows = ~O.near_tie_rows(p, cfg.num_experts_per_tok, rel=1e-4)
+    ids_equal = bool(torch.equal(idx.cpu().long()[ok_rows], ridx[ok_rows]))
+    local_ok = st["finite"] and st["max_abs_over_bf16"] <= 2e-2 and st["mean_rel"] <= 5e-3
+    vals = torch.tensor([st["max_abs_over_bf16"], st["mean_rel"], 0.0 if local_ok else 1.0,
+                         0.0 if ids_equal else 1.0], device=x.device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    return {"ok": bool(vals[2].item() == 0.0 and vals[3].item() == 0.0), "tokens_per_rank": n,
+            "max_abs_over_bf16": float(vals[0]), "mean_rel": float(vals[1]),
+            "router_ids_equal_outside_near_ties": bool(vals[3].item() == 0.0),
+            "tolerance": "max_abs_over_bf16 <= 2e-2, mean_rel <= 5e-3 vs fp32 oracle"}
+
+
 def run_reference(args, world, rank):
     """--impl reference: the reference's own CPU path on the host cores, rank 0 only."""
-    from qwen3_5_vl_cuda_custom_b200 import synthetic as syn
-    from qwen3_5_vl_cuda_custom_b200.configs import a3b_moe_text
     if rank != 0:
         return
-    cfg = a3b_moe_text(1)
-    S = args.tokens
-    g = torch.Generator().manual_seed(1)
-    P = syn.layer_params(cfg, g)
-    x = syn.hidden_states((1, S, cfg.hidden_size), g)
-    pos = syn.text_positions(1, S)
+    w = make_workload(args.workload, 1, 0, args.tokens)
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    step = cpu_reference_step_fn(cfg, P, x, pos, torch.bfloat16)
-    kind = "reference"
+    sample = 4096 if w.name == "c2" else 2048
+    step, n = cpu_reference_layer(w, torch.bfloat16, sample)
     if step is None:
         print(json.dumps({"impl": "reference", "unavailable":
                           "reference package not installed under baseline/_ref"}))
         return
-    ts = time_cpu(step, max(1, min(args.warmup, 2)), max(1, args.steps))
+    ts = time_cpu(step, max(1, min(args.warmup, 2)), max(3, args.steps))
     t = statistics.median(ts)
-    value = S / t
+    value = n / t
     line = {
-        "impl": "reference", "metric": "moe_layer_prefill_tokens_per_s", "value": value,
+        "impl": "reference", "metric": METRIC, "value": value,
         "unit": "tokens/s", "n_gpus": args.gpus, "steps": len(ts), "warmup": args.warmup,
-        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": t * 1e3, "higher_is_better": True, "scaling": w.scaling,
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "C2 30B-A3B MoE decoder layer prefill, 1x4096 tokens",
-                   "tokens_per_step": S, "device": "cpu"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": kind,
-                         "sample": f"full step: one layer over {S} tokens, bf16, median of {len(ts)}"},
+        "config": {"workload": w.desc, "tokens_per_step": n, "device": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "sample": f"one layer over {n} tokens, bf16, median of {len(ts)}"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 def run_ours(args, world, rank, local):
-    from qwen3_5_vl_cuda_custom_b200 import build, kernels as K
-    from qwen3_5_vl_cuda_custom_b200 import synthetic as syn
-    from qwen3_5_vl_cuda_custom_b200.configs import a3b_moe_text
+    from qwen3_5_vl_cuda_custom_b200 import build, kernels as K, _lib
     build.build()
     dev = torch.device("cuda", local)
-    cfg = a3b_moe_text(1)
-    S = args.tokens
-    T = S
+    w = make_workload(args.workload, world, rank, args.tokens)
+    cfg = w.cfg
     ep_group = None
     if world > 1:
         import torch.distributed as dist
         ep_group = dist.group.WORLD
-    layer, rot, P, g = build_layer(cfg, 1, dev, ep_group)
-    if world > 1:  # each rank prefills its own sequence
-        g = torch.Generator().manual_seed(1000 + rank)
-    x_cpu = syn.hidden_states((1, S, cfg.hidden_size), g)
-    x = x_cpu.to(dev, torch.bfloat16)
-    pos_cpu = syn.text_positions(1, S)
-    pos = pos_cpu.to(dev)
+    layer, rot = build_layer(w, dev, ep_group)
+    x = c4_embedding_input(w, dev) if w.x_cpu is None else w.x_cpu.to(dev, torch.bfloat16)
+    if w.x_cpu is None:
+        w.x_cpu = x.float().cpu()
+    B, S, _ = x.shape
+    T = B * S
+    pos = w.pos_cpu.to(dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
     bpos = rot.bind(pos)
+    link_gbs = measure_link(world, rank, dev) if world > 1 else None
 
     with torch.no_grad(), ClockSampler(local) as clk:
         clk.wait_first()
-        # ---------------- warm-up (the library is AOT-built: no JIT here)
         for _ in range(max(3, args.warmup)):
             layer(x, bpos)
         barrier(world)
-        # ---------------- device-timed steps: eager module calls, then the
-        # same forward replayed from a CUDA graph (GraphedDecoderLayer)
         from qwen3_5_vl_cuda_custom_b200.graphs import GraphedDecoderLayer
 
         def timed(step_fn):
@@ -374,21 +592,14 @@ def run_ours(args, world, rank, local):
             return allreduce_max(sum(a.elapsed_time(b) for a, b in times), world)
 
         eager_ms = timed(lambda: layer(x, bpos))
-
-        # ---------------- per-stage breakdown (same kernels, events between)
-        samples: dict[str, list[float]] = {}
-        for _ in range(7):
-            flush.zero_()
-            marks = []
-            staged_forward(layer, rot, x, pos, marks)
-            torch.cuda.synchronize()
-            for (_, a), (name, b) in zip(marks[:-1], marks[1:]):
-                samples.setdefault(name, []).append(a.elapsed_time(b))
-        stage_ms = {k: statistics.median(v) for k, v in samples.items()}
+        stage_ms = stage_breakdown(layer, rot, x, pos, flush, world)
 
         graphed = None
+        launches_per_step = None
         try:
-            graphed = GraphedDecoderLayer(layer, rot, x, pos)
+            n0 = _lib.query("q35_launch_count")
+            graphed = GraphedDecoderLayer(layer, rot, x, pos, warmup=0)
+            launches_per_step = _lib.query("q35_launch_count") - n0
             total_ms = timed(graphed.replay)
         except Exception as e:  # capture unsupported here: report the eager time
             print(f"graph capture failed ({type(e).__name__}: {e}); eager timing", file=sys.stderr)
@@ -397,14 +608,17 @@ def run_ours(args, world, rank, local):
         mode = "CUDA-graph replay" if graphed is not None else "eager"
         if graphed is not None and total_ms > eager_ms:
             total_ms, mode = eager_ms, "eager"  # the faster of the two module paths
+        if launches_per_step is None or mode == "eager":
+            n0 = _lib.query("q35_launch_count")
+            layer(x, bpos)
+            launches_per_step = _lib.query("q35_launch_count") - n0
         ms_per_step = total_ms / args.steps
-        value = world * T * args.steps / (total_ms / 1e3)
-        eager_value = world * T * args.steps / (eager_ms / 1e3)
+        value = w.tokens_global * args.steps / (total_ms / 1e3)
+        eager_value = w.tokens_global * args.steps / (eager_ms / 1e3)
 
         # ---------------- end to end through the public API: each step copies its
-        # input from pinned host memory and its output back.  One GPU: the
-        # StreamedLayerRunner overlaps the copies with neighbouring replays.
-        x_host = x_cpu.to(torch.bfloat16).pin_memory()
+        # input from pinned host memory and its output back.
+        x_host = x.cpu().pin_memory()
         out_host = torch.empty_like(x_host).pin_memory()
         if graphed is not None:
             from qwen3_5_vl_cuda_custom_b200.graphs import StreamedLayerRunner
@@ -424,9 +638,10 @@ def run_ours(args, world, rank, local):
         e1.record()
         barrier(world)
         e2e_ms = allreduce_max(e0.elapsed_time(e1), world)
-        e2e_value = world * T * args.steps / (e2e_ms / 1e3)
+        e2e_value = w.tokens_global * args.steps / (e2e_ms / 1e3)
 
     K.device_error_check()
+    parity = ep_parity(layer, rot, w, x, pos, world) if world > 1 else None
 
     peaks, peak_src = load_peaks()
     table = stage_table(cfg, T, S, world)
@@ -437,10 +652,6 @@ def run_ours(args, world, rank, local):
         achieved = amount / t_top / 1e12
         peak = peaks["bf16_tflops"]
         unit = "TFLOP/s"
-    elif bound == "link":
-        achieved = amount * (world - 1) / world / t_top / 1e9
-        peak = LINK_GBS
-        unit = "GB/s"
     else:
         achieved = amount / t_top / 1e9
         peak = peaks["hbm_gbs"]
@@ -448,10 +659,8 @@ def run_ours(args, world, rank, local):
     breakdown = {}
     for name, ms in stage_ms.items():
         b, a = table[name]
-        if b == "link":
-            a = a * (world - 1) / world
         rate = a / (ms / 1e3) / (1e12 if b == "tensor" else 1e9)
-        pk = {"tensor": peaks["bf16_tflops"], "link": LINK_GBS}.get(b, peaks["hbm_gbs"])
+        pk = peaks["bf16_tflops"] if b == "tensor" else peaks["hbm_gbs"]
         breakdown[name] = {"ms": round(ms, 4), "bound": b,
                            "achieved": round(rate, 1), "frac": round(rate / pk, 3)}
 
@@ -459,33 +668,23 @@ def run_ours(args, world, rank, local):
         return
     cpu = None
     if not args.no_cpu_baseline and world == 1:
-        threads = os.cpu_count() or 1
-        torch.set_num_threads(threads)
-        step = cpu_reference_step_fn(cfg, P, x_cpu, pos_cpu, torch.bfloat16)
-        kind, sample = "reference", f"reference CudaTextDecoderLayer on CPU, bf16, {S} tokens, median of 2 after 1 warm-up"
-        if step is None:
-            from oracle import layer_oracle as O
-            kind, sample = "port", f"oracle fp32 layer on CPU, {S} tokens"
-
-            def step():
-                return O.decoder_layer(x_cpu, P, cfg, pos_cpu)["out"]
-        ts = time_cpu(step, 1, 2)
-        cpu = {"value": S / statistics.median(ts), "unit": "tokens/s", "cores": threads,
-               "kind": kind, "sample": sample}
+        cpu = cpu_baseline(w)
     clocks = clk.summary()
     in_bytes = x_host.numel() * 2
+    c2_full = w.name == "c2" and S == 4096 and world == 1
     line = {
-        "metric": "moe_layer_prefill_tokens_per_s", "value": value, "unit": "tokens/s",
+        "metric": METRIC, "value": value, "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup),
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": w.scaling,
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "C2 30B-A3B MoE decoder layer prefill, 1x4096 tokens per GPU",
+        "config": {"workload": w.desc,
                    "hidden": cfg.hidden_size, "heads": f"{cfg.num_heads}/{cfg.num_kv_heads}x{cfg.head_dim}",
                    "experts": f"{cfg.num_experts} top-{cfg.num_experts_per_tok} I={cfg.moe_intermediate_size}",
-                   "tokens_per_gpu": T, "global_batch": world, "seq_len": S,
-                   "parallelism": (f"ep{world}: {cfg.num_experts // world} experts/GPU, NCCL "
-                                   f"all-to-all; dp{world} attention over sequences"
+                   "tokens_per_gpu": T, "global_batch": w.tokens_global // S, "seq_len": S,
+                   "parallelism": (f"ep{world}: {cfg.num_experts // world} experts/GPU; "
+                                   f"dp{world} attention over sequences"
                                    if world > 1 else "1 GPU, all experts local"),
+                   "router_skew": "0.5*log Zipf(1.2)" if w.bias is not None else None,
                    "mode": mode,
                    "l2": "256 MiB flush between timed steps"},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": in_bytes,
@@ -493,22 +692,26 @@ def run_ours(args, world, rank, local):
                 "api": "StreamedLayerRunner(GraphedDecoderLayer)"},
         "eager": {"value": eager_value, "ms_per_step": eager_ms / args.steps,
                   "note": "same layer through the module API without graph replay"},
-        "gpu_launches": LAUNCHES_PER_LAYER * args.steps,
+        "gpu_launches": int(launches_per_step) * args.steps,
         "roofline": {"bound": bound, "kernel": top, "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak,
-                     "traffic": TRAFFIC_BYTES_C2.get(top) if S == 4096 else None,
+                     "traffic": TRAFFIC_BYTES_C2.get(top) if c2_full else None,
                      "algorithmic": amount,
-                     "algorithmic_bytes": ALGO_BYTES_C2.get(top) if S == 4096 else None,
+                     "algorithmic_bytes": ALGO_BYTES_C2.get(top) if c2_full else None,
                      # the kernel's own lower bound max(FLOPs / tensor peak, bytes / HBM peak)
                      # over its measured time (a weight-streaming GEMM can be either)
                      "frac_of_bound": (max(amount / (peaks["bf16_tflops"] * 1e12) if bound == "tensor" else 0.0,
                                            (ALGO_BYTES_C2.get(top) or 0.0) / (peaks["hbm_gbs"] * 1e9))
-                                       / t_top) if S == 4096 else None,
+                                       / t_top) if c2_full else None,
                      "peak_source": peak_src},
         "breakdown": breakdown,
+        "breakdown_note": "device-only: each stage replayed from its own CUDA graph after an L2 flush",
         "cpu_baseline": cpu,
         "clocks": clocks,
     }
+    if world > 1:
+        line["parity"] = parity
+        line["link_gbs_measured"] = link_gbs
     print(json.dumps(line), flush=True)
 
 
@@ -522,9 +725,13 @@ def run_c3(args, local):
     from qwen3_5_vl_cuda_custom_b200.kv_cache import LayerKVCache
     build.build()
     dev = torch.device("cuda", local)
-    cfg = a3b_moe_text(1)
+    w = Workload()
+    w.cfg = cfg = a3b_moe_text(1)
+    g = torch.Generator().manual_seed(2)
+    w.P = syn.layer_params(cfg, g)
+    w.bias = None
     B, past = 64, 8192
-    layer, rot, P, g = build_layer(cfg, 2, dev)
+    layer, rot = build_layer(w, dev)
     cache = LayerKVCache(B, cfg.num_kv_heads, past + 1, cfg.head_dim, dev)
     gen = torch.Generator(device=dev).manual_seed(2)
     cache.k[:, :, :past].normal_(generator=gen)
@@ -599,11 +806,12 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--tokens", type=int, default=4096)
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="sequence length override (c2: 4096, c4/c5: 2048)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["c2", "c3"], default="c2",
-                    help="c2: the headline prefill layer (default); c3: decode over a KV cache "
-                         "(one GPU, informational line)")
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2",
+                    help="c2: the headline prefill layer (default); c4: 8x2048 strong scaling "
+                         "with a skewed router; c5: multimodal 4x2048; c3: decode (one GPU)")
     args = ap.parse_args()
     if args.workload == "c3":
         run_c3(args, int(os.environ.get("LOCAL_RANK", "0")))

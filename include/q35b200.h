@@ -63,6 +63,11 @@ Q35_API const char *q35_version(void);
  * the collective kernels of an overlapped expert-parallel exchange -- keeps
  * some SMs.  No reference counterpart.                                     */
 Q35_API int q35_set_sm_limit(int n);
+/* Number of kernel launches this library has issued in this process (all
+ * devices, all threads).  A CUDA-graph capture issues launches too, so the
+ * difference across a capture is the number of library kernels in the graph.
+ * No reference counterpart.                                                */
+Q35_API int64_t q35_launch_count(void);
 
 /* ---- RMSNorm ------------------------------------------------------------
  * y[r,:] = bf16( x[r,:] * rsqrt(mean(x[r,:]^2) + eps) * w ), fp32 inside.

@@ -22,6 +22,7 @@ _SIGS = {
     "q35_device_error_check": (c_int, [_i32p]),
     "q35_version": (c_char_p, []),
     "q35_set_sm_limit": (c_int, [c_int]),
+    "q35_launch_count": (c_int64, []),
     "q35_rmsnorm_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
     "q35_qknorm_mrope_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, _i32p, c_int,
                                      c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int,
@@ -43,6 +44,21 @@ _SIGS = {
     "q35_moe_permute_workspace": (c_int64, [c_int64, c_int]),
     "q35_moe_permute": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_void_p, c_void_p, c_void_p]),
+    "q35_moe_permute_slabs": (c_int, [c_void_p, c_int, c_int64, c_void_p, c_int, c_int, c_void_p,
+                                      c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "q35_ep_window_bytes": (c_int64, [c_int, c_int64, c_int64, c_int]),
+    "q35_ep_window_offsets": (c_int, [c_int, c_int64, c_int64, c_int, POINTER(c_int64)]),
+    "q35_ep_window_alloc": (c_int, [c_int, c_int64, c_int64, c_int, POINTER(c_void_p)]),
+    "q35_ep_window_free": (c_int, [c_void_p]),
+    "q35_ep_ipc_handle": (c_int, [c_void_p, c_void_p]),
+    "q35_ep_ipc_open": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "q35_ep_ipc_close": (c_int, [c_void_p]),
+    "q35_ep_set_peers": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int, c_void_p]),
+    "q35_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_int, c_int,
+                                c_int, c_int64, c_void_p, c_void_p, c_void_p]),
+    "q35_ep_wait": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64, c_void_p]),
+    "q35_ep_return": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int64, c_int, c_int, c_void_p,
+                              c_void_p]),
     "q35_moe_permute_noalloc_max_workspace": (c_int64, []),
     "q35_moe_permute_noalloc": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_void_p, c_void_p]),

@@ -4,6 +4,7 @@
 #include <stdarg.h>
 #include <stdio.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -120,9 +121,14 @@ int make_tmap_bf16_2d(CUtensorMap *map, const void *base, uint64_t inner,
   return Q35_OK;
 }
 
+std::atomic<long long> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 }  // namespace q35
 
 extern "C" {
+
+int64_t q35_launch_count(void) { return q35::g_launches.load(); }
 
 const char *q35_status_string(int status) {
   switch (status) {

@@ -25,6 +25,8 @@ int num_sms();
 // device, once (cached per device and kernel) so launches inside CUDA-graph
 // capture make no attribute calls.
 int ensure_smem_attr(const void *kernel, int bytes);
+// Counts one kernel launch issued by this library (read by q35_launch_count).
+void count_launch();
 
 #define Q35_CHECK_CUDA(expr)                                   \
   do {                                                         \
@@ -34,6 +36,7 @@ int ensure_smem_attr(const void *kernel, int bytes);
 
 #define Q35_LAUNCH_CHECK(what)                                   \
   do {                                                           \
+    ::q35::count_launch();                                       \
     cudaError_t _e = cudaGetLastError();                         \
     if (_e != cudaSuccess) return ::q35::cuda_fail(_e, what);    \
   } while (0)

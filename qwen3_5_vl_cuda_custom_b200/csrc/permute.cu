@@ -25,13 +25,27 @@ namespace {
 constexpr int kChunk = 128;  // tokens per chunk (one thread each)
 constexpr int kTileM = 128;  // grouped-GEMM M tile
 
+// Row t takes part when t < T and, for slab-structured input (slab_cnt !=
+// nullptr: rows [s * slab_rows, s * slab_rows + slab_cnt[s]) of slab s are
+// filled, the rest hold stale data), when it lies in the filled part of its
+// slab.
+__device__ __forceinline__ bool row_valid(int64_t t, int64_t T,
+                                          const int32_t *__restrict__ slab_cnt,
+                                          int64_t slab_rows) {
+  if (t >= T) return false;
+  if (slab_cnt == nullptr) return true;
+  return (t % slab_rows) < static_cast<int64_t>(slab_cnt[t / slab_rows]);
+}
+
 __device__ __forceinline__ void build_masks(const int32_t *__restrict__ idx,
                                             int64_t T, int k, int E,
-                                            uint32_t (*mask)[4], int *err) {
+                                            uint32_t (*mask)[4], int *err,
+                                            const int32_t *__restrict__ slab_cnt,
+                                            int64_t slab_rows) {
   for (int i = threadIdx.x; i < E * 4; i += blockDim.x) mask[i >> 2][i & 3] = 0u;
   __syncthreads();
   const int64_t t = static_cast<int64_t>(blockIdx.x) * kChunk + threadIdx.x;
-  if (t < T) {
+  if (row_valid(t, T, slab_cnt, slab_rows)) {
     for (int j = 0; j < k; ++j) {
       const int e = idx[t * k + j];
       if (e < 0) continue;  // empty slot (expert-parallel receive side)
@@ -47,10 +61,11 @@ __device__ __forceinline__ void build_masks(const int32_t *__restrict__ idx,
 
 __global__ void __launch_bounds__(kChunk) permute_count_kernel(
     const int32_t *__restrict__ idx, int64_t T, int k, int E,
-    int32_t *__restrict__ chunk_counts, int *err) {
+    int32_t *__restrict__ chunk_counts, int *err,
+    const int32_t *__restrict__ slab_cnt, int64_t slab_rows) {
   extern __shared__ uint32_t smem_mask[];
   auto mask = reinterpret_cast<uint32_t(*)[4]>(smem_mask);
-  build_masks(idx, T, k, E, mask, err);
+  build_masks(idx, T, k, E, mask, err, slab_cnt, slab_rows);
   for (int e = threadIdx.x; e < E; e += blockDim.x)
     chunk_counts[static_cast<int64_t>(blockIdx.x) * E + e] =
         __popc(mask[e][0]) + __popc(mask[e][1]) + __popc(mask[e][2]) +
@@ -107,12 +122,13 @@ __global__ void __launch_bounds__(kChunk) permute_scatter_kernel(
     const int32_t *__restrict__ idx, int64_t T, int k, int E,
     const int32_t *__restrict__ chunk_base, const int32_t *__restrict__ offsets,
     int32_t *__restrict__ sorted_tok, int32_t *__restrict__ slot_pos,
-    int *err) {
+    int *err, const int32_t *__restrict__ slab_cnt, int64_t slab_rows) {
   extern __shared__ uint32_t smem_mask[];
   auto mask = reinterpret_cast<uint32_t(*)[4]>(smem_mask);
-  build_masks(idx, T, k, E, mask, nullptr);  // errors reported by the count pass
+  // errors are reported by the count pass
+  build_masks(idx, T, k, E, mask, nullptr, slab_cnt, slab_rows);
   const int64_t t = static_cast<int64_t>(blockIdx.x) * kChunk + threadIdx.x;
-  if (t >= T) return;
+  if (!row_valid(t, T, slab_cnt, slab_rows)) return;
   const int w = threadIdx.x >> 5, b = threadIdx.x & 31;
   for (int j = 0; j < k; ++j) {
     const int e = idx[t * k + j];
@@ -289,11 +305,12 @@ extern "C" int64_t q35_moe_permute_workspace(int64_t T, int E) {
   return chunks * static_cast<int64_t>(E > 0 ? E : 1);
 }
 
-extern "C" int q35_moe_permute(const int32_t *idx, int64_t T, int k, int E,
-                               int32_t *counts, int32_t *offsets,
-                               int32_t *sorted_tok, int32_t *slot_pos,
-                               int32_t *tile_offsets, int32_t *workspace,
-                               q35_stream_t stream) {
+namespace {
+int permute_impl(const int32_t *idx, int64_t T, int k, int E, int32_t *counts,
+                 int32_t *offsets, int32_t *sorted_tok, int32_t *slot_pos,
+                 int32_t *tile_offsets, int32_t *workspace,
+                 const int32_t *slab_cnt, int64_t slab_rows,
+                 q35_stream_t stream) {
   if (!counts || !offsets || !tile_offsets || !workspace ||
       (T > 0 && (!idx || !sorted_tok || !slot_pos)))
     return fail(Q35_ERR_INVALID, "moe_permute: null pointer");
@@ -309,7 +326,7 @@ extern "C" int q35_moe_permute(const int32_t *idx, int64_t T, int k, int E,
   const size_t smem = static_cast<size_t>(E) * 4 * sizeof(uint32_t);
   if (chunks > 0) {
     permute_count_kernel<<<static_cast<unsigned>(chunks), kChunk, smem, s>>>(
-        idx, T, k, E, workspace, err);
+        idx, T, k, E, workspace, err, slab_cnt, slab_rows);
     Q35_LAUNCH_CHECK("permute count launch");
   }
   permute_scan_kernel<<<1, 1024, 0, s>>>(workspace, chunks, E, counts, offsets,
@@ -317,10 +334,35 @@ extern "C" int q35_moe_permute(const int32_t *idx, int64_t T, int k, int E,
   Q35_LAUNCH_CHECK("permute scan launch");
   if (chunks > 0) {
     permute_scatter_kernel<<<static_cast<unsigned>(chunks), kChunk, smem, s>>>(
-        idx, T, k, E, workspace, offsets, sorted_tok, slot_pos, err);
+        idx, T, k, E, workspace, offsets, sorted_tok, slot_pos, err, slab_cnt,
+        slab_rows);
     Q35_LAUNCH_CHECK("permute scatter launch");
   }
   return Q35_OK;
+}
+}  // namespace
+
+extern "C" int q35_moe_permute(const int32_t *idx, int64_t T, int k, int E,
+                               int32_t *counts, int32_t *offsets,
+                               int32_t *sorted_tok, int32_t *slot_pos,
+                               int32_t *tile_offsets, int32_t *workspace,
+                               q35_stream_t stream) {
+  return permute_impl(idx, T, k, E, counts, offsets, sorted_tok, slot_pos,
+                      tile_offsets, workspace, nullptr, 0, stream);
+}
+
+extern "C" int q35_moe_permute_slabs(const int32_t *idx, int n_slabs,
+                                     int64_t slab_rows, const int32_t *slab_cnt,
+                                     int k, int E, int32_t *counts,
+                                     int32_t *offsets, int32_t *sorted_tok,
+                                     int32_t *slot_pos, int32_t *tile_offsets,
+                                     int32_t *workspace, q35_stream_t stream) {
+  if (!slab_cnt) return fail(Q35_ERR_INVALID, "moe_permute_slabs: null slab counts");
+  if (n_slabs < 1 || slab_rows < 1)
+    return fail(Q35_ERR_SHAPE, "moe_permute_slabs: %d slabs of %lld rows", n_slabs,
+                (long long)slab_rows);
+  return permute_impl(idx, n_slabs * slab_rows, k, E, counts, offsets, sorted_tok,
+                      slot_pos, tile_offsets, workspace, slab_cnt, slab_rows, stream);
 }
 
 extern "C" int q35_gather_rows(const void *src, const int32_t *rows, void *dst,
@@ -488,7 +530,7 @@ extern "C" int q35_moe_permute_noalloc(const int32_t *idx, int64_t T, int k,
   // that word is allocated on first use, which this entry point must not do.
   if (chunks > 0) {
     permute_count_kernel<<<static_cast<unsigned>(chunks), kChunk, smem, s>>>(
-        idx, T, k, E, scratch, nullptr);
+        idx, T, k, E, scratch, nullptr, nullptr, 0);
     Q35_LAUNCH_CHECK("permute_noalloc count launch");
   }
   permute_scan_kernel<<<1, 1024, 0, s>>>(scratch, chunks, E, counts, offsets,
@@ -496,7 +538,7 @@ extern "C" int q35_moe_permute_noalloc(const int32_t *idx, int64_t T, int k,
   Q35_LAUNCH_CHECK("permute_noalloc scan launch");
   if (chunks > 0) {
     permute_scatter_kernel<<<static_cast<unsigned>(chunks), kChunk, smem, s>>>(
-        idx, T, k, E, scratch, offsets, sorted_tok, slot_pos, nullptr);
+        idx, T, k, E, scratch, offsets, sorted_tok, slot_pos, nullptr, nullptr, 0);
     Q35_LAUNCH_CHECK("permute_noalloc scatter launch");
   }
   return Q35_OK;

@@ -249,6 +249,31 @@ def moe_permute(idx: torch.Tensor, num_experts: int) -> Permutation:
     return Permutation(counts, offsets, sorted_tok, slot_pos, tile_offsets, num_experts)
 
 
+def moe_permute_slabs(idx: torch.Tensor, n_slabs: int, slab_rows: int, slab_cnt: torch.Tensor,
+                      num_experts: int) -> Permutation:
+    """moe_permute over slab-structured rows: idx (n_slabs*slab_rows, k) int32 where
+    only the first slab_cnt[s] rows of slab s take part (the expert-parallel
+    receive window); rows past a slab's count are ignored whatever they hold."""
+    idx = _require(idx, "moe_permute_slabs.idx", torch.int32)
+    slab_cnt = _require(slab_cnt, "moe_permute_slabs.slab_cnt", torch.int32)
+    R, k = idx.shape
+    if R != n_slabs * slab_rows:
+        raise RuntimeError(f"moe_permute_slabs: {R} rows for {n_slabs} slabs of {slab_rows}")
+    dev = idx.device
+    i32 = dict(device=dev, dtype=torch.int32)
+    counts = torch.empty(num_experts, **i32)
+    offsets = torch.empty(num_experts + 1, **i32)
+    tile_offsets = torch.empty(num_experts + 1, **i32)
+    sorted_tok = torch.empty(R * k, **i32)
+    slot_pos = torch.empty(R * k, **i32)
+    ws = torch.empty(max(1, _lib.query("q35_moe_permute_workspace", R, num_experts)), **i32)
+    with torch.cuda.device(dev):
+        _lib.call("q35_moe_permute_slabs", idx.data_ptr(), n_slabs, slab_rows, slab_cnt.data_ptr(),
+                  k, num_experts, counts.data_ptr(), offsets.data_ptr(), sorted_tok.data_ptr(),
+                  slot_pos.data_ptr(), tile_offsets.data_ptr(), ws.data_ptr(), _stream(idx))
+    return Permutation(counts, offsets, sorted_tok, slot_pos, tile_offsets, num_experts)
+
+
 def gather_rows(src: torch.Tensor, rows: torch.Tensor, n_dev: torch.Tensor | None = None) -> torch.Tensor:
     """dst[r] = src[rows[r]] for bf16 rows (rows int32); n_dev (device int32) bounds r."""
     src = _require(src, "gather_rows.src")
@@ -541,7 +566,7 @@ def device_error_check():
 
 __all__ = [
     "rmsnorm", "matmul", "softmax", "cuda_topk", "cuda_index_add", "swiglu", "residual_add",
-    "router_topk", "router_split_weights", "pack_b_tiles", "moe_permute", "Permutation", "gather_rows", "grouped_gateup_swiglu",
+    "router_topk", "router_split_weights", "pack_b_tiles", "moe_permute", "moe_permute_slabs", "Permutation", "gather_rows", "grouped_gateup_swiglu",
     "grouped_down", "moe_combine", "qknorm_mrope", "mrope", "attention_tokens",
     "flash_attention", "attention_cache", "kv_append", "device_error_check", "default_scale",
     "layernorm", "gelu_tanh", "apply_rope", "conv3d_patch",

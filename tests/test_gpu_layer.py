@@ -312,3 +312,41 @@ def test_streamed_runner_copies_in_and_out():
     with torch.no_grad():
         ref, _, _ = layer(x.to(DEV), rot.bind(pos))
     assert torch.equal(out_host, ref.cpu())
+
+
+def test_c4_skewed_router_layer():
+    """Config 4's layer shape and skew: 8 x 2048 tokens with router logits
+    biased by 0.5*log Zipf(1.2) popularity (seed 3), so one expert holds
+    thousands of rows in the grouped GEMMs.  The GPU runs the whole batch; the
+    oracle checks two of the sequences (a token's MoE math does not depend on
+    the other tokens), routing ids and offsets on the full batch."""
+    from qwen3_5_vl_cuda_custom_b200 import synthetic as syn, kernels as K
+    from qwen3_5_vl_cuda_custom_b200.configs import a3b_moe_text
+    cfg = a3b_moe_text(1)
+    g = torch.Generator().manual_seed(3)
+    P = syn.layer_params(cfg, g)
+    bias = syn.zipf_router_bias(cfg.num_experts, g)
+    B, S = 8, 2048
+    x = syn.hidden_states((B, S, cfg.hidden_size), g)
+    pos = syn.text_positions(B, S)
+    layer = make_layer(cfg, P)
+    layer.mlp.router_bias = bias.to(DEV)
+    rot = rotary(cfg)
+    xd, posd = x.to(DEV, torch.bfloat16), pos.to(DEV)
+    with torch.no_grad():
+        y, rl, _ = layer(xd, rot.bind(posd))
+        h = layer.self_attn(layer.input_layernorm(xd), rot.bind(posd), residual=xd,
+                            out_dtype=torch.float32)[0]
+        m_in = layer.post_attention_layernorm(h).reshape(-1, cfg.hidden_size)
+        _, idx, _ = layer.mlp.route(m_in)
+        counts = K.moe_permute(idx, cfg.num_experts).counts.cpu()
+    assert int(counts.max()) >= 2000, counts.max()  # a hot expert: thousands of rows
+    assert int(counts.sum()) == B * S * cfg.num_experts_per_tok
+    check_routing(layer, h, cfg, bias=bias)
+    sub = [1, 6]
+    gidx = idx.cpu().reshape(B, S, -1)[sub].reshape(-1, cfg.num_experts_per_tok)
+    ref = O.decoder_layer(x[sub], P, cfg, pos[:, sub], router_bias=bias)
+    check(h[sub], ref["h_attn"], "attention + residual")
+    check_layer_output(y[sub], ref, gidx, cfg,
+                       lambda fi: O.decoder_layer(x[sub], P, cfg, pos[:, sub], router_bias=bias,
+                                                  force_idx=fi), "C4 skewed layer")
