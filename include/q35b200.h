@@ -228,6 +228,67 @@ Q35_API int q35_ep_scatter(const void *x, const int32_t *idx, const float *w, in
                            float *meta_w, int64_t meta_slab, int32_t *ret_pos,
                            q35_stream_t stream);
 
+/* q35_moe_permute over slab-structured rows: idx int32 [n_slabs*slab_rows, k]
+ * where only rows [s*slab_rows, s*slab_rows + slab_cnt[s]) of slab s take
+ * part (slab_cnt int32 [n_slabs] in device memory); the other rows are
+ * ignored whatever they hold and their slot_pos entries are left untouched.
+ * Outputs sized for n_slabs*slab_rows rows.  This is the receive side of the
+ * peer-memory expert-parallel exchange, where slab s holds the rows rank s
+ * sent.  No reference counterpart (the reference has no expert parallelism). */
+Q35_API int q35_moe_permute_slabs(const int32_t *idx, int n_slabs, int64_t slab_rows,
+                                  const int32_t *slab_cnt, int k, int E, int32_t *counts,
+                                  int32_t *offsets, int32_t *sorted_tok, int32_t *slot_pos,
+                                  int32_t *tile_offsets, int32_t *workspace,
+                                  q35_stream_t stream);
+
+/* ---- Expert-parallel exchange over peer memory (NVLink) -----------------
+ * No reference counterpart: the reference runs every expert on one GPU
+ * (REF cuda_qwen3_vl/modules/moe.py:71-83).  N ranks (one process per GPU),
+ * rank r owns experts [r*El, (r+1)*El).  Each rank allocates one exchange
+ * window (q35_ep_window_alloc, sized by N, Tcap = max tokens per rank and
+ * call, H, k), exports it with q35_ep_ipc_handle, opens every peer's handle
+ * with q35_ep_ipc_open and stores the N base addresses (its own at index r)
+ * with q35_ep_set_peers.  One forward is then, on every rank, in stream order:
+ *   q35_ep_dispatch  token rows + slot lists into the owners' windows,
+ *                    ret_pos int32 [T, N] = d*Tcap + t where rank d will
+ *                    return token t's partial, else -1;
+ *   q35_ep_wait(0)   until every rank's rows have arrived;
+ *   q35_moe_permute_slabs / gather / grouped GEMMs on the window's slabs
+ *                    (offsets from q35_ep_window_offsets: rows, ret, idx,
+ *                    wts, tok, cnt, flags, ctrl, peers, total bytes);
+ *   q35_ep_return    each received row's weighted partial (slot_pos of that
+ *                    permutation, y the grouped down output) into the
+ *                    sender's window;
+ *   q35_ep_wait(1)   until every rank's partials have arrived;
+ *   q35_moe_combine  y = the window's ret area, weights 1, slot_pos = ret_pos,
+ *                    k = N: adds each token's partials to its residual.
+ * Every rank must issue the same sequence of calls.  Waits give up after
+ * limit_ns and record DEV_ERR_WAIT_TIMEOUT (site 310 dispatch, 311 return) in
+ * the device error word; dispatch reports an expert id >= N*El at site 301.
+ * N <= 32, k <= 32, H % 8 == 0, T <= Tcap.                                   */
+Q35_API int64_t q35_ep_window_bytes(int N, int64_t Tcap, int64_t H, int k);
+Q35_API int q35_ep_window_offsets(int N, int64_t Tcap, int64_t H, int k, int64_t *out10);
+Q35_API int q35_ep_window_alloc(int N, int64_t Tcap, int64_t H, int k, void **window);
+Q35_API int q35_ep_window_free(void *window);
+Q35_API int q35_ep_ipc_handle(void *window, void *handle64);
+Q35_API int q35_ep_ipc_open(const void *handle64, void **peer_window);
+Q35_API int q35_ep_ipc_close(void *peer_window);
+Q35_API int q35_ep_set_peers(void *window, int N, int64_t Tcap, int64_t H, int k,
+                             const uint64_t *peer_bases);
+Q35_API int q35_ep_dispatch(const void *x, const int32_t *idx, const float *w, int64_t T, int k,
+                            int64_t H, int El, int N, int rank, int64_t Tcap, void *window,
+                            int32_t *ret_pos, q35_stream_t stream);
+Q35_API int q35_ep_wait(void *window, int N, int64_t Tcap, int64_t H, int k, int which,
+                        int64_t limit_ns, q35_stream_t stream);
+Q35_API int q35_ep_return(const void *y, const int32_t *slot_pos, int64_t Tcap, int k, int64_t H,
+                          int N, int rank, void *window, q35_stream_t stream);
+
+/* Self-test of the bounded waits (no reference counterpart): one kernel
+ * waits on an mbarrier phase that nothing completes, gives up after limit_ns
+ * (0 < limit_ns <= 2 s), records DEV_ERR_WAIT_TIMEOUT at site 901 (a = the
+ * microseconds waited) in the device error word and returns.               */
+Q35_API int q35_selftest_wait_timeout(int64_t limit_ns, q35_stream_t stream);
+
 /* dst[r,:] = src[rows[r],:] for r < n (bf16, cols % 8 == 0); n may be read
  * from device memory (n_dev != NULL: *n_dev rows, at most n_max).           */
 Q35_API int q35_gather_rows(const void *src, const int32_t *rows, void *dst,

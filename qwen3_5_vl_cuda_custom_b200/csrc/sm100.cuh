@@ -50,13 +50,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits until the phase with `parity` has completed.  Returns false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Waits until the phase with `parity` has completed.  Returns false once
+// `limit_ns` of polling has passed without it.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0 && global_timer_ns() - t0 > kWaitLimitNs) return false;
+    if ((it & 255u) == 0 && global_timer_ns() - t0 > limit_ns) return false;
   }
 }
 

@@ -11,11 +11,20 @@ outputs to static buffers; ``__call__`` copies the caller's input in, replays,
 and returns the static outputs (overwritten by the next call).  Weights are
 read where they live: in-place updates are seen by later replays, replacing a
 parameter tensor requires a new capture.
+
+With a preallocated ``LayerKVCache`` as ``past_kv`` the captured forward
+appends its rows at the cache offset of capture time and attends over that
+fixed length: a replay rewrites the same positions and does NOT advance
+``cache.length``.  The cache length is restored after the warm-up and the
+capture, so the cache reads as it did before construction.  This suits a
+fixed-position step (a benchmark); a decode loop needs one capture per
+position, or the eager module.
 """
 from __future__ import annotations
 
 import torch
 
+from .kv_cache import KVCache, LayerKVCache
 from .modules import CudaTextDecoderLayer, TextMRoPE
 
 
@@ -27,17 +36,27 @@ class GraphedDecoderLayer:
         self.layer = layer
         self.static_x = example_x.detach().clone()
         self.static_pos = position_ids.detach().clone()
+        if isinstance(past_kv, KVCache):
+            raise RuntimeError("GraphedDecoderLayer captures one layer: pass that layer's "
+                               "LayerKVCache, not the model's KVCache")
         self.past_kv = past_kv
+        length0 = past_kv.length if isinstance(past_kv, LayerKVCache) else None
         bound = rotary.bind(self.static_pos)
         side = torch.cuda.Stream(device=example_x.device)
         side.wait_stream(torch.cuda.current_stream(example_x.device))
         with torch.no_grad(), torch.cuda.stream(side):
             for _ in range(warmup):  # caches (fused weights, TMA attributes) filled outside capture
+                if length0 is not None:
+                    past_kv.length = length0
                 layer(self.static_x, bound, past_kv=past_kv)
         torch.cuda.current_stream(example_x.device).wait_stream(side)
         self.graph = torch.cuda.CUDAGraph()
+        if length0 is not None:
+            past_kv.length = length0
         with torch.no_grad(), torch.cuda.graph(self.graph):
             self.static_out = layer(self.static_x, bound, past_kv=past_kv)
+        if length0 is not None:
+            past_kv.length = length0
 
     def replay(self):
         """Replays the captured forward on the current static input."""

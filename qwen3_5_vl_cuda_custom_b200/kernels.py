@@ -99,12 +99,20 @@ def matmul(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
 
 _SM_COUNT: dict[int, int] = {}
 
+# Split-K for decode-sized dense GEMMs (M <= 128 rows).  It changes the fp32
+# summation order of a row's dot products, so the same row projected in a
+# call of <= 128 rows and in a larger call can differ in the last bits (within
+# the GEMM tolerance; batch invariance is lost).  Set to False for runs that
+# must give bit-identical rows whatever the call size.
+DECODE_SPLITK = True
+
 
 def _splitk_factor(M: int, N: int, K: int, device) -> int:
     """K splits for a dense GEMM of at most 128 rows: the largest power of two
     (<= 16) that divides the 64-wide k-blocks and keeps ceil(N/128) * splits
-    CTAs within one wave; 1 (no split) for larger M or when it would not help."""
-    if M == 0 or M > 128 or K % 64 != 0 or N % 32 != 0:
+    CTAs within one wave; 1 (no split) for larger M, when it would not help,
+    or when DECODE_SPLITK is off."""
+    if not DECODE_SPLITK or M == 0 or M > 128 or K % 64 != 0 or N % 32 != 0:
         return 1
     idx = device.index if device.index is not None else torch.cuda.current_device()
     sms = _SM_COUNT.get(idx)

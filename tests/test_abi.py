@@ -62,3 +62,30 @@ def test_ops_refuse_cpu_tensors():
     from qwen3_5_vl_cuda_custom_b200 import kernels as K
     with pytest.raises(RuntimeError, match="CUDA tensor required"):
         K.rmsnorm(torch.ones(2, 8, dtype=torch.bfloat16), torch.ones(8, dtype=torch.bfloat16))
+
+
+def test_ep_window_layout(lib):
+    """Exchange-window offsets: ordered, 256-byte aligned, sized for the slabs."""
+    N, Tcap, H, k = 8, 4096, 2048, 8
+    offs = (ctypes.c_int64 * 10)()
+    assert lib.q35_ep_window_offsets(N, Tcap, H, k, offs) == 0
+    o = list(offs)
+    assert o == sorted(o) and all(v % 256 == 0 for v in o)
+    rows, ret, idx, wts, tok, cnt, flags, ctrl, peers, total = o
+    assert ret - rows >= N * Tcap * H * 2 and idx - ret >= N * Tcap * H * 2
+    assert wts - idx >= N * Tcap * k * 4 and tok - wts >= N * Tcap * k * 4
+    assert total == lib.q35_ep_window_bytes(N, Tcap, H, k)
+    assert lib.q35_ep_window_offsets(33, Tcap, H, k, offs) == 2  # N <= 32
+    assert lib.q35_ep_window_offsets(N, Tcap, 2047, k, offs) == 2  # H % 8
+    assert lib.q35_ep_window_bytes(0, Tcap, H, k) == -1
+
+
+def test_ep_and_selftest_validation(lib):
+    p = ctypes.c_void_p(256)  # never dereferenced: validation fails first
+    # T above the window's capacity
+    assert lib.q35_ep_dispatch(p, p, p, 5000, 8, 2048, 16, 8, 0, 4096, p, p, None) == 2
+    assert lib.q35_ep_wait(p, 8, 4096, 2048, 8, 2, 1000, None) == 1  # which
+    assert lib.q35_ep_wait(p, 8, 4096, 2048, 8, 0, 0, None) == 1  # limit
+    assert lib.q35_selftest_wait_timeout(0, None) == 1
+    assert lib.q35_selftest_wait_timeout(3_000_000_000, None) == 1
+    assert lib.q35_moe_permute_slabs(p, 0, 16, p, 8, 128, p, p, p, p, p, p, None) == 2

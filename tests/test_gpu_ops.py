@@ -70,6 +70,30 @@ def test_gemm_splitk_with_residual_and_fp32_out(M):
         err = (out.float().cpu() - ref).abs().max()
         assert err <= 1e-2 * ref.abs().max() + 1e-3, float(err)
 
+def test_gemm_splitk_agrees_with_unsplit_on_same_rows():
+    """The split-K path (decode-sized calls) and the single-pass path (what the
+    same rows get inside a larger call) agree within the GEMM tolerance; with
+    DECODE_SPLITK off a small call is bit-identical to the same rows of a
+    large call."""
+    g = gen(777)
+    N, K_ = 5120, 2048
+    a = bf(torch.randn(300, K_, generator=g)).to(DEV)
+    b = bf(torch.randn(N, K_, generator=g) * 0.02).to(DEV)
+    Kk = K()
+    big = Kk.matmul(a, b)  # 300 rows: no split
+    assert Kk._splitk_factor(64, N, K_, torch.device(DEV)) > 1
+    small = Kk.matmul(a[:64].contiguous(), b)
+    ref = a[:64].float() @ b.float().t()
+    assert (small.float() - big[:64].float()).abs().max() <= 1e-2 * ref.abs().max() + 1e-3
+    try:
+        Kk.DECODE_SPLITK = False
+        assert Kk._splitk_factor(64, N, K_, torch.device(DEV)) == 1
+        unsplit = Kk.matmul(a[:64].contiguous(), b)
+    finally:
+        Kk.DECODE_SPLITK = True
+    assert torch.equal(unsplit, big[:64])
+
+
 @pytest.mark.parametrize("M,N,K_", [(8, 64, 64), (128, 128, 64), (300, 384, 256), (4096, 5120, 2048),
                                     (4096, 2048, 4096), (1, 256, 128), (129, 2048, 768),
                                     (64, 5120, 2048), (64, 2048, 4096), (3, 96, 640)])
