@@ -57,8 +57,9 @@ sys.path.insert(0, str(ROOT))
 # read, outputs written).  Only C2 has captures.
 TRAFFIC_BYTES_C2 = {"gate_up_swiglu": 1055.5e6, "down": 575.9e6, "attention": 42.9e6}
 ALGO_BYTES_C2 = {"gate_up_swiglu": 989.8e6, "down": 587.2e6, "attention": 75.5e6}
-# NVLink peer copy per direction measured on this pool's B200s (used only when
-# the run cannot measure its own figure, i.e. at N = 1)
+# NVLink peer copy per direction, the pool's measured reference figure (the
+# denominator of the "link" stages; the run also reports its own NCCL
+# send/recv figure as link_gbs_measured)
 LINK_GBS_POOL = 770.0
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 METRIC = "moe_layer_prefill_tokens_per_s"
@@ -242,6 +243,13 @@ def stage_table(cfg, T: int, S: int, world: int = 1) -> dict:
         "combine_residual": ("hbm", T * k * H * 2 + T * H * 4 + T * H * 2 + T * k * 4),
         # expert parallel: dispatch + experts + return + combine in one stage
         "moe_expert_parallel": ("tensor", T * k * 2 * 3 * H * I),
+        # peer-memory transport: rows that cross NVLink each way (expected
+        # ranks per token N(1 - (1 - 1/N)^k), the own rank's share local)
+        "ep_prepare": ("hbm", 0),
+        "ep_dispatch": ("link", T * H * 2 * world * (1 - (1 - 1 / world) ** k) * (world - 1) / world),
+        "ep_experts": ("tensor", T * k * 2 * 3 * H * I),
+        "ep_return": ("link", T * H * 2 * world * (1 - (1 - 1 / world) ** k) * (world - 1) / world),
+        "ep_combine": ("hbm", T * world * H * 2 + T * H * 4 + T * H * 2),
     }
 
 
@@ -290,9 +298,15 @@ def layer_stages(layer, rot, x, pos):
         st["logits"], st["idx"], st["wts"] = moe.route(st["m2"])
 
     if getattr(moe, "exchange", None) is not None:
-        @add("moe_expert_parallel")
-        def _(st):
-            st["out"] = moe.experts(st["m2"], st["idx"], st["wts"], st["h"].reshape(-1, H))
+        if moe.transport == "p2p":
+            @add("ep_prepare")
+            def _(st):
+                st.update(x2d=st["m2"], weights=st["wts"], residual=st["h"].reshape(-1, H))
+            stages.extend(moe.p2p_stages())
+        else:
+            @add("moe_expert_parallel")
+            def _(st):
+                st["out"] = moe.experts(st["m2"], st["idx"], st["wts"], st["h"].reshape(-1, H))
         return stages, st
 
     @add("permute")
@@ -697,7 +711,7 @@ def run_ours(args, world, rank, local):
 
     peaks, peak_src = load_peaks()
     table = stage_table(cfg, T, S, world)
-    top = max(stage_ms, key=stage_ms.get)
+    top = max((n_ for n_ in stage_ms if table[n_][0] != "link"), key=stage_ms.get)
     bound, amount = table[top]
     t_top = stage_ms[top] / 1e3
     if bound == "tensor":
@@ -712,7 +726,7 @@ def run_ours(args, world, rank, local):
     for name, ms in stage_ms.items():
         b, a = table[name]
         rate = a / (ms / 1e3) / (1e12 if b == "tensor" else 1e9)
-        pk = peaks["bf16_tflops"] if b == "tensor" else peaks["hbm_gbs"]
+        pk = {"tensor": peaks["bf16_tflops"], "link": LINK_GBS_POOL}.get(b, peaks["hbm_gbs"])
         breakdown[name] = {"ms": round(ms, 4), "bound": b,
                            "achieved": round(rate, 1), "frac": round(rate / pk, 3)}
 
@@ -765,6 +779,8 @@ def run_ours(args, world, rank, local):
     if world > 1:
         line["parity"] = parity
         line["link_gbs_measured"] = link_gbs
+        line["link_note"] = ("link stages are divided by the pool's 770 GB/s peer-copy figure; "
+                             "link_gbs_measured is NCCL send/recv of 256 MiB between rank pairs")
     print(json.dumps(line), flush=True)
 
 

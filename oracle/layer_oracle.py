@@ -216,6 +216,57 @@ def decoder_layer(x: torch.Tensor, P: dict, cfg, position_ids, past_kv=None,
                 h_attn=h, moe_in=m_in)
 
 
+def swiglu_mlp(x: torch.Tensor, P: dict, prefix: str = "mlp.") -> torch.Tensor:
+    """CudaSwiGLUMLP.forward in fp32 (REF modules/mlp.py:19-22):
+    down(silu(gate(x)) * up(x)); REF kernels/swiglu.py:57-58 for the product."""
+    x = x.float()
+    g = linear(x, P[prefix + "gate_proj.weight"], P.get(prefix + "gate_proj.bias"))
+    u = linear(x, P[prefix + "up_proj.weight"], P.get(prefix + "up_proj.bias"))
+    return linear(F.silu(g) * u, P[prefix + "down_proj.weight"], P.get(prefix + "down_proj.bias"))
+
+
+def dense_decoder_layer(x: torch.Tensor, P: dict, cfg, position_ids, past_kv=None,
+                        interleaved: bool = False):
+    """CudaTextDecoderLayer.forward for a dense (non-MoE) layer in fp32
+    (REF modules/text_decoder.py:51-65 with the MLP branch)."""
+    x = x.float()
+    eps = cfg.rms_norm_eps
+    a, (k, v) = attention_block(rmsnorm(x, P["input_layernorm.weight"], eps), P, cfg,
+                                position_ids, past_kv, interleaved)
+    h = x + a
+    out = h + swiglu_mlp(rmsnorm(h, P["post_attention_layernorm.weight"], eps), P)
+    return dict(out=out, k=k, v=v, h_attn=h)
+
+
+def text_model(input_ids: torch.Tensor, P: dict, cfg, moe_layers, position_ids=None,
+               force_idx=None):
+    """CudaQwen3VLMoeModel.forward (text only) in fp32 (REF models/moe.py:59-73,
+    85-97): embedding lookup (REF modules/embedding.py:26-27), the decoder
+    layers, the final RMSNorm and lm_head.  ``moe_layers[i]`` says whether
+    layer i is an MoE layer; ``force_idx[j]`` (optional) is the j-th MoE
+    layer's top-k choice (see ``moe``).  Returns dict(logits, router_logits)."""
+    B, S = input_ids.shape
+    x = P["embed_tokens.weight"].float()[input_ids]
+    if position_ids is None:
+        pos = torch.arange(S).unsqueeze(0).expand(B, S)
+        position_ids = torch.stack([pos, pos, pos], dim=0)
+    rls = []
+    mi = 0
+    for i, is_moe in enumerate(moe_layers):
+        pre = f"layers.{i}."
+        Pl = {k[len(pre):]: v for k, v in P.items() if k.startswith(pre)}
+        if is_moe:
+            fi = None if force_idx is None else force_idx[mi]
+            r = decoder_layer(x, Pl, cfg, position_ids, force_idx=fi)
+            rls.append(r["router_logits"])
+            mi += 1
+        else:
+            r = dense_decoder_layer(x, Pl, cfg, position_ids)
+        x = r["out"]
+    hidden = rmsnorm(x, P["norm.weight"], cfg.rms_norm_eps)
+    return dict(logits=linear(hidden, P["lm_head.weight"]), router_logits=rls)
+
+
 def near_tie_rows(probs: torch.Tensor, k: int, rel: float = 1e-5) -> torch.Tensor:
     """Rows where two neighbours among the sorted top-(k+1) probabilities differ
     by less than rel * the larger one: a logit computed in another summation

@@ -246,30 +246,65 @@ class ExpertParallelSparseMoE(CudaSparseMoE):
             self._ones = torch.ones(T, N, device=device, dtype=torch.float32)
         return self._ones[:T]
 
-    def _experts_p2p(self, x2d, idx, weights, residual):
-        T, H = x2d.shape
-        k = idx.shape[1]
+    def p2p_stages(self):
+        """The peer-memory expert path as (name, fn(state)) stages, in order:
+        ``ep_dispatch`` (rows into the owners' windows, wait for every rank's
+        rows), ``ep_experts`` (permutation, gather, grouped GEMMs on the
+        received slabs), ``ep_return`` (partials into the senders' windows,
+        wait for every rank's partials), ``ep_combine`` (partials + residual).
+        ``state`` holds x2d, idx, weights and residual on entry and ``out`` on
+        exit.  ``experts`` runs them back to back; the benchmark times them
+        one by one."""
         ex = self.exchange
         N, El, rank = ex.world, ex.E_local, ex.rank
-        dev = x2d.device
-        win = _window_for(ex.group, dev, N, rank, T, H, k, self.ep_max_tokens)
-        Tc = win.Tcap
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        ret_pos = torch.empty(T, N, device=dev, dtype=torch.int32)
-        with torch.cuda.device(dev):
-            _lib.call("q35_ep_dispatch", x2d.data_ptr(), idx.data_ptr(), weights.data_ptr(), T, k, H,
-                      El, N, rank, Tc, win.ptr, ret_pos.data_ptr(), stream)
-            _lib.call("q35_ep_wait", win.ptr, N, Tc, H, k, 0, WAIT_LIMIT_NS, stream)
-        lperm = K.moe_permute_slabs(win.idx, N, Tc, win.cnt, El)
-        # only offsets[El] of the N*Tcap*k slots hold an expert of this rank
-        xs = K.gather_rows(win.rows, lperm.sorted_tok, n_dev=lperm.offsets[El:])
-        act = K.grouped_gateup_swiglu(xs, self.gate_up_proj, lperm)
-        y = K.grouped_down(act, self.down_proj, lperm)
-        with torch.cuda.device(dev):
-            _lib.call("q35_ep_return", y.data_ptr(), lperm.slot_pos.data_ptr(), Tc, k, H, N, rank,
-                      win.ptr, stream)
-            _lib.call("q35_ep_wait", win.ptr, N, Tc, H, k, 1, WAIT_LIMIT_NS, stream)
-        return K.moe_combine(win.ret, self._ones_like(T, N, dev), ret_pos, residual, T, H)
+
+        def dispatch(st):
+            x2d, idx, w = st["x2d"], st["idx"], st["weights"]
+            T, H = x2d.shape
+            k = idx.shape[1]
+            dev = x2d.device
+            win = _window_for(ex.group, dev, N, rank, T, H, k, self.ep_max_tokens)
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            ret_pos = torch.empty(T, N, device=dev, dtype=torch.int32)
+            with torch.cuda.device(dev):
+                _lib.call("q35_ep_dispatch", x2d.data_ptr(), idx.data_ptr(), w.data_ptr(), T, k, H,
+                          El, N, rank, win.Tcap, win.ptr, ret_pos.data_ptr(), stream)
+                _lib.call("q35_ep_wait", win.ptr, N, win.Tcap, H, k, 0, WAIT_LIMIT_NS, stream)
+            st["win"], st["ret_pos"] = win, ret_pos
+
+        def experts(st):
+            win = st["win"]
+            lperm = K.moe_permute_slabs(win.idx, N, win.Tcap, win.cnt, El)
+            # only offsets[El] of the N*Tcap*k slots hold an expert of this rank
+            xs = K.gather_rows(win.rows, lperm.sorted_tok, n_dev=lperm.offsets[El:])
+            act = K.grouped_gateup_swiglu(xs, self.gate_up_proj, lperm)
+            st["y"] = K.grouped_down(act, self.down_proj, lperm)
+            st["slot_pos"] = lperm.slot_pos
+
+        def ret(st):
+            win, y = st["win"], st["y"]
+            H, k, Tc = win.H, win.k, win.Tcap
+            dev = y.device
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            with torch.cuda.device(dev):
+                _lib.call("q35_ep_return", y.data_ptr(), st["slot_pos"].data_ptr(), Tc, k, H, N, rank,
+                          win.ptr, stream)
+                _lib.call("q35_ep_wait", win.ptr, N, Tc, H, k, 1, WAIT_LIMIT_NS, stream)
+
+        def combine(st):
+            T, H = st["x2d"].shape
+            dev = st["x2d"].device
+            st["out"] = K.moe_combine(st["win"].ret, self._ones_like(T, N, dev), st["ret_pos"],
+                                      st["residual"], T, H)
+
+        return [("ep_dispatch", dispatch), ("ep_experts", experts), ("ep_return", ret),
+                ("ep_combine", combine)]
+
+    def _experts_p2p(self, x2d, idx, weights, residual):
+        st = {"x2d": x2d, "idx": idx, "weights": weights, "residual": residual}
+        for _, fn in self.p2p_stages():
+            fn(st)
+        return st["out"]
 
     # ------------------------------------------------------------ nccl transport
     ep_chunks = 2  # token chunks whose exchange overlaps the other chunk's experts
@@ -350,9 +385,11 @@ class ExpertParallelSparseMoE(CudaSparseMoE):
         return out
 
     def experts(self, x2d: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor,
-                residual: torch.Tensor | None = None) -> torch.Tensor:
+                residual: torch.Tensor | None = None, chunk_counts=None) -> torch.Tensor:
         """Expert compute for routed tokens across the group: (T,H) -> (T,H),
-        the weighted combine plus ``residual`` (if given) included."""
+        the weighted combine plus ``residual`` (if given) included.
+        ``chunk_counts`` is accepted for signature compatibility and unused:
+        the receiving ranks permute what they receive."""
         if self.transport == "p2p":
             try:
                 return self._experts_p2p(x2d, idx.contiguous(), weights.contiguous(), residual)
