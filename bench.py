@@ -293,11 +293,16 @@ def layer_stages(layer, rot, x, pos):
         st["m2"] = K.rmsnorm(st["h"], layer.post_attention_layernorm.weight,
                              layer.post_attention_layernorm.eps).reshape(-1, H)
 
+    ep = getattr(moe, "exchange", None) is not None
+
     @add("router")
     def _(st):
-        st["logits"], st["idx"], st["wts"] = moe.route(st["m2"])
+        if ep:
+            st["logits"], st["idx"], st["wts"] = moe.route(st["m2"])
+        else:
+            st["logits"], st["idx"], st["wts"], st["cc"] = moe.route(st["m2"], chunk_counts=True)
 
-    if getattr(moe, "exchange", None) is not None:
+    if ep:
         if moe.transport == "p2p":
             @add("ep_prepare")
             def _(st):
@@ -311,7 +316,10 @@ def layer_stages(layer, rot, x, pos):
 
     @add("permute")
     def _(st):
-        st["perm"] = K.moe_permute(st["idx"], moe.num_experts)
+        if st["cc"] is not None:
+            st["perm"] = K.moe_permute_counted(st["idx"], st["cc"], moe.num_experts)
+        else:
+            st["perm"] = K.moe_permute(st["idx"], moe.num_experts)
 
     @add("gather")
     def _(st):

@@ -228,6 +228,29 @@ Q35_API int q35_ep_scatter(const void *x, const int32_t *idx, const float *w, in
                            float *meta_w, int64_t meta_slab, int32_t *ret_pos,
                            q35_stream_t stream);
 
+/* Tensor-core router in two launches (replaces the matmul -> softmax -> topk
+ * chain of REF modules/moe.py:60-65, csrc/softmax_op.cu:8-53 and
+ * csrc/moe_routing_op.cu:11-63 for supported shapes): x bf16 [T, H],
+ * w3 = q35_router_split_weights(gate) bf16 [E, 3H], bias fp32 [E] or NULL.
+ * Outputs as q35_router_topk_fwd, and, if chunk_counts != NULL, int32
+ * [ceil(T/128), E]: per 128-token chunk the number of tokens routed to each
+ * expert (the permutation's count pass, for q35_moe_permute_counted).
+ * Supported when q35_router_fused_supported(T, H, E, k): H % 256 == 0,
+ * E in {32, 64, 128}, 1 <= k <= min(16, E).  Logits are summed in a fixed
+ * order (deterministic); ties go to the lower expert id.                    */
+Q35_API int q35_router_fused_supported(int64_t T, int H, int E, int k);
+Q35_API int q35_router_topk_fused(const void *x, const void *w3, const float *bias,
+                                  float *logits, int32_t *idx, float *weights,
+                                  int32_t *chunk_counts, int64_t T, int H, int E, int k,
+                                  int renorm, q35_stream_t stream);
+
+/* q35_moe_permute from the router's chunk_counts in one launch, no workspace:
+ * the same outputs bit for bit (REF modules/moe.py:71-76 ordering).         */
+Q35_API int q35_moe_permute_counted(const int32_t *idx, int64_t T, int k, int E,
+                                    const int32_t *chunk_counts, int32_t *counts,
+                                    int32_t *offsets, int32_t *sorted_tok, int32_t *slot_pos,
+                                    int32_t *tile_offsets, q35_stream_t stream);
+
 /* q35_moe_permute over slab-structured rows: idx int32 [n_slabs*slab_rows, k]
  * where only rows [s*slab_rows, s*slab_rows + slab_cnt[s]) of slab s take
  * part (slab_cnt int32 [n_slabs] in device memory); the other rows are

@@ -45,6 +45,11 @@ _SIGS = {
     "q35_moe_permute_workspace": (c_int64, [c_int64, c_int]),
     "q35_moe_permute": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_void_p, c_void_p, c_void_p]),
+    "q35_router_fused_supported": (c_int, [c_int64, c_int, c_int, c_int]),
+    "q35_router_topk_fused": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                      c_void_p, c_int64, c_int, c_int, c_int, c_int, c_void_p]),
+    "q35_moe_permute_counted": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_void_p,
+                                        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "q35_moe_permute_slabs": (c_int, [c_void_p, c_int, c_int64, c_void_p, c_int, c_int, c_void_p,
                                       c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "q35_ep_window_bytes": (c_int64, [c_int, c_int64, c_int64, c_int]),

@@ -198,11 +198,22 @@ def router_split_weights(gate_weight: torch.Tensor) -> torch.Tensor:
     return w3
 
 
+def router_fused_supported(T: int, H: int, E: int, k: int) -> bool:
+    """Whether the tensor-core cluster router (q35_router_topk_fused) takes this
+    shape: H a multiple of 256, E in (32, 64, 128), k <= 16."""
+    return bool(_lib.query("q35_router_fused_supported", T, H, E, k))
+
+
 def router_topk(x2d: torch.Tensor, gate_weight: torch.Tensor, top_k: int, renorm: bool = True,
-                bias: torch.Tensor | None = None, gate_split: torch.Tensor | None = None):
+                bias: torch.Tensor | None = None, gate_split: torch.Tensor | None = None,
+                chunk_counts: bool = False):
     """Fused fp32 router: logits (T,E) fp32, top-k ids (T,k) int32, weights (T,k) fp32.
     With ``gate_split`` (router_split_weights(gate_weight)) the logits run on the
-    tensor cores (exact bf16 products, fp32 accumulation)."""
+    tensor cores (exact bf16 products, fp32 accumulation); supported shapes take
+    the cluster kernel, which also counts the permutation's chunk counts.
+    ``chunk_counts=True`` returns a fourth value: the per-128-token-chunk expert
+    counts [ceil(T/128), E] int32 for moe_permute_counted, or None when the
+    shape takes another router path."""
     x2d = _require(x2d, "router.x")
     wg = _require(gate_weight, "router.gate_weight", torch.float32)
     T, H = x2d.shape
@@ -212,6 +223,15 @@ def router_topk(x2d: torch.Tensor, gate_weight: torch.Tensor, top_k: int, renorm
     w = torch.empty(T, top_k, device=x2d.device, dtype=torch.float32)
     if bias is not None:
         bias = _require(bias, "router.bias", torch.float32)
+    if gate_split is not None and router_fused_supported(T, H, E, top_k):
+        gate_split = _require(gate_split, "router.gate_split")
+        cc = (torch.empty(max(1, -(-T // 128)), E, device=x2d.device, dtype=torch.int32)
+              if chunk_counts else None)
+        with torch.cuda.device(x2d.device):
+            _lib.call("q35_router_topk_fused", x2d.data_ptr(), gate_split.data_ptr(), _ptr(bias),
+                      logits.data_ptr(), idx.data_ptr(), w.data_ptr(), _ptr(cc), T, H, E,
+                      int(top_k), 1 if renorm else 0, _stream(x2d))
+        return (logits, idx, w, cc) if chunk_counts else (logits, idx, w)
     ws = None
     if gate_split is not None:
         gate_split = _require(gate_split, "router.gate_split")
@@ -221,7 +241,7 @@ def router_topk(x2d: torch.Tensor, gate_weight: torch.Tensor, top_k: int, renorm
         _lib.call("q35_router_topk_fwd", x2d.data_ptr(), wg.data_ptr(), _ptr(gate_split), _ptr(bias),
                   logits.data_ptr(), idx.data_ptr(), w.data_ptr(), T, H, E, int(top_k),
                   1 if renorm else 0, _ptr(ws), _stream(x2d))
-    return logits, idx, w
+    return (logits, idx, w, None) if chunk_counts else (logits, idx, w)
 
 
 class Permutation:
@@ -254,6 +274,29 @@ def moe_permute(idx: torch.Tensor, num_experts: int) -> Permutation:
         _lib.call("q35_moe_permute", idx.data_ptr(), T, k, num_experts, counts.data_ptr(),
                   offsets.data_ptr(), sorted_tok.data_ptr(), slot_pos.data_ptr(),
                   tile_offsets.data_ptr(), ws.data_ptr(), _stream(idx))
+    return Permutation(counts, offsets, sorted_tok, slot_pos, tile_offsets, num_experts)
+
+
+def moe_permute_counted(idx: torch.Tensor, chunk_counts: torch.Tensor, num_experts: int) -> Permutation:
+    """moe_permute from the router's per-chunk expert counts (router_topk with
+    chunk_counts=True): one launch instead of count + scan + scatter, the same
+    bit-exact result."""
+    idx = _require(idx, "moe_permute_counted.idx", torch.int32)
+    cc = _require(chunk_counts, "moe_permute_counted.chunk_counts", torch.int32)
+    T, k = idx.shape
+    if tuple(cc.shape) != (max(1, -(-T // 128)), num_experts):
+        raise RuntimeError(f"moe_permute_counted: chunk_counts {tuple(cc.shape)} for T={T}")
+    dev = idx.device
+    i32 = dict(device=dev, dtype=torch.int32)
+    counts = torch.empty(num_experts, **i32)
+    offsets = torch.empty(num_experts + 1, **i32)
+    tile_offsets = torch.empty(num_experts + 1, **i32)
+    sorted_tok = torch.empty(T * k, **i32)
+    slot_pos = torch.empty(T * k, **i32)
+    with torch.cuda.device(dev):
+        _lib.call("q35_moe_permute_counted", idx.data_ptr(), T, k, num_experts, cc.data_ptr(),
+                  counts.data_ptr(), offsets.data_ptr(), sorted_tok.data_ptr(), slot_pos.data_ptr(),
+                  tile_offsets.data_ptr(), _stream(idx))
     return Permutation(counts, offsets, sorted_tok, slot_pos, tile_offsets, num_experts)
 
 
@@ -574,7 +617,7 @@ def device_error_check():
 
 __all__ = [
     "rmsnorm", "matmul", "softmax", "cuda_topk", "cuda_index_add", "swiglu", "residual_add",
-    "router_topk", "router_split_weights", "pack_b_tiles", "moe_permute", "moe_permute_slabs", "Permutation", "gather_rows", "grouped_gateup_swiglu",
+    "router_topk", "router_split_weights", "pack_b_tiles", "moe_permute", "moe_permute_slabs", "moe_permute_counted", "router_fused_supported", "Permutation", "gather_rows", "grouped_gateup_swiglu",
     "grouped_down", "moe_combine", "qknorm_mrope", "mrope", "attention_tokens",
     "flash_attention", "attention_cache", "kv_append", "device_error_check", "default_scale",
     "layernorm", "gelu_tanh", "apply_rope", "conv3d_patch",

@@ -365,17 +365,24 @@ class CudaSparseMoE(nn.Module):
             self._pack_cache = cache
         return cache[1], cache[2]
 
-    def route(self, x2d: torch.Tensor):
-        """Router only: (logits fp32 (T,E), top-k ids int32 (T,k), weights fp32 (T,k))."""
+    def route(self, x2d: torch.Tensor, chunk_counts: bool = False):
+        """Router only: (logits fp32 (T,E), top-k ids int32 (T,k), weights fp32 (T,k));
+        with ``chunk_counts`` also the per-chunk expert counts for the one-launch
+        permutation (None when the shape takes another router path)."""
         return K.router_topk(x2d, self.gate_weight, self.top_k, self.norm_topk_prob,
-                             bias=self.router_bias, gate_split=self._gate_split())
+                             bias=self.router_bias, gate_split=self._gate_split(),
+                             chunk_counts=chunk_counts)
 
     def experts(self, x2d: torch.Tensor, idx: torch.Tensor, weights: torch.Tensor,
-                residual: torch.Tensor | None = None) -> torch.Tensor:
+                residual: torch.Tensor | None = None,
+                chunk_counts: torch.Tensor | None = None) -> torch.Tensor:
         """Expert compute + weighted combine for routed tokens (T,H) -> (T,H)."""
         T, H = x2d.shape
         gu_p, dn_p = self._packed_experts()
-        perm = K.moe_permute(idx, self.num_experts)
+        if chunk_counts is not None:
+            perm = K.moe_permute_counted(idx, chunk_counts, self.num_experts)
+        else:
+            perm = K.moe_permute(idx, self.num_experts)
         xs = K.gather_rows(x2d, perm.sorted_tok)
         act = K.grouped_gateup_swiglu(xs, self.gate_up_proj, perm, w_packed=gu_p)
         y = K.grouped_down(act, self.down_proj, perm, w_packed=dn_p)
@@ -384,9 +391,13 @@ class CudaSparseMoE(nn.Module):
     def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None):
         B, S, H = x.shape
         x2d = x.reshape(-1, H)
-        logits, idx, w = self.route(x2d)
         res2d = None if residual is None else residual.reshape(-1, H)
-        out = self.experts(x2d, idx, w, res2d)
+        if getattr(self, "exchange", None) is None:
+            logits, idx, w, cc = self.route(x2d, chunk_counts=True)
+            out = self.experts(x2d, idx, w, res2d, chunk_counts=cc)
+        else:  # expert parallel: the receiving ranks permute what they receive
+            logits, idx, w = self.route(x2d)
+            out = self.experts(x2d, idx, w, res2d)
         return out.reshape(B, S, H), logits
 
 

@@ -164,6 +164,42 @@ def test_router_tensor_core_path(T, H, E, k):
     assert (w.cpu()[ok] - rw[ok]).abs().max() < 1e-5
 
 
+@pytest.mark.parametrize("T,H,E,k", [(4096, 2048, 128, 8), (16384, 2048, 128, 8), (77, 256, 32, 4),
+                                     (300, 512, 64, 8), (1, 2048, 128, 8), (129, 1024, 128, 8)])
+def test_router_fused_and_counted_permutation(T, H, E, k):
+    """Cluster router (three exact bf16 planes in TMEM, partials reduced over
+    distributed shared memory) with the permutation's chunk counts, then the
+    one-launch scan + scatter: logits vs the fp32 oracle, ids and weights
+    outside near ties, chunk counts and the whole permutation bit-exact."""
+    Kk = K()
+    assert Kk.router_fused_supported(T, H, E, k)
+    g = gen(T * 7 + E + H)
+    x = bf(torch.randn(T, H, generator=g))
+    wg = torch.randn(E, H, generator=g) * 0.02
+    bias = torch.randn(E, generator=g) * 0.1
+    w3 = Kk.router_split_weights(wg.to(DEV))
+    logits, idx, w, cc = Kk.router_topk(x.to(DEV), wg.to(DEV), k, bias=bias.to(DEV), gate_split=w3,
+                                        chunk_counts=True)
+    assert cc is not None and tuple(cc.shape) == (-(-T // 128), E)
+    rl, p, ridx, rw = O.router(x.float(), wg, k, bias=bias)
+    assert (logits.cpu() - rl).abs().max() < 2e-5
+    ok = ~O.near_tie_rows(p, k, rel=1e-4)
+    assert torch.equal(idx.cpu().long()[ok], ridx[ok])
+    assert (w.cpu()[ok] - rw[ok]).abs().max() < 1e-5
+    gi = idx.cpu().numpy()
+    want = np.stack([np.bincount(gi[c * 128:(c + 1) * 128].reshape(-1), minlength=E)
+                     for c in range(-(-T // 128))])
+    assert cc.cpu().numpy().tolist() == want.tolist()
+    perm = Kk.moe_permute_counted(idx, cc, E)
+    counts, offsets, sorted_tok, slot_pos, tiles = O.permutation(gi, E)
+    assert perm.counts.cpu().numpy().tolist() == counts.tolist()
+    assert perm.offsets.cpu().numpy().tolist() == offsets.tolist()
+    assert perm.sorted_tok.cpu().numpy().tolist() == sorted_tok.tolist()
+    assert perm.slot_pos.cpu().numpy().tolist() == slot_pos.tolist()
+    assert perm.tile_offsets.cpu().numpy().tolist() == tiles.tolist()
+    Kk.device_error_check()
+
+
 def test_router_ties_to_lower_index():
     """All-equal logits: every expert ties; the top-k must be 0..k-1."""
     x = torch.zeros(4, 256, dtype=torch.bfloat16, device=DEV)
