@@ -472,6 +472,21 @@ Q35_API int q35_conv3d_patch_fwd(const void *patches, const void *w, const void 
                                  void *out, int64_t n_patches, int64_t embed, int64_t K,
                                  q35_stream_t stream);
 
+/* Vision attention input (replaces the qkv reshape + apply_rope pair of
+ * REF modules/attention.py:31-39): qkv bf16 [S, 3, H, D] (the fused projection
+ * with its bias) -> q, k, v bf16 [H, S, Dp], Dp >= D, zero-padded, with the
+ * rotate-half rotary over all D dims of q and k; angles fp32 [S, D/2]: the
+ * angle of dims j and j + D/2 (fp32 sin/cos).  Padding lets head dims the
+ * attention kernels do not take (72 in Qwen3-VL's vision tower) run on the
+ * head_dim 128 kernels.                                                     */
+Q35_API int q35_vision_qkv_rope_pad(const void *qkv, const float *angles, void *q, void *k,
+                                    void *v, int64_t S, int H, int D, int Dp,
+                                    q35_stream_t stream);
+/* Token-major [S, H, Dp] -> [S, H, D]: drops the head padding of the
+ * attention output (no reference counterpart; the reference needs no padding). */
+Q35_API int q35_unpad_heads(const void *x, void *y, int64_t S, int H, int D, int Dp,
+                            q35_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -23,6 +23,9 @@ _SIGS = {
     "q35_version": (c_char_p, []),
     "q35_set_sm_limit": (c_int, [c_int]),
     "q35_launch_count": (c_int64, []),
+    "q35_vision_qkv_rope_pad": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
+                                        c_int, c_int, c_int, c_void_p]),
+    "q35_unpad_heads": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p]),
     "q35_selftest_wait_timeout": (c_int, [c_int64, c_void_p]),
     "q35_rmsnorm_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
     "q35_qknorm_mrope_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, _i32p, c_int,

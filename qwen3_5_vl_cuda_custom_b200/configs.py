@@ -1,8 +1,8 @@
 """Text-stack configuration, with the reference's field names.
 
 Mirrors ``TextConfig`` / ``MoETextConfig`` / ``Qwen3VLConfig`` of
-REF cuda_qwen3_vl/configs/config.py:26-115 (vision fields are kept only so a
-reference config object converts; the vision tower is not built here), plus
+REF cuda_qwen3_vl/configs/config.py:9-115 (``VisionConfig`` drives the vision
+tower of ``vision.py``), plus
 the five benchmark shapes used by the tests and the bench harness.
 """
 from __future__ import annotations

@@ -116,6 +116,59 @@ __global__ void __launch_bounds__(256) rope_kernel(const uint16_t *__restrict__ 
   st8(y + row * D + d0, v);
 }
 
+// Vision attention input: the fused projection qkv [S, 3, H, D] (bias already
+// added) -> head-major q, k, v [H, S, Dp] with Dp >= D zero-padded, and the
+// 2-D rotary on q and k over all D dims (rotate-half, half = D/2; angle of
+// dims j and j + D/2 = ang[s, j], REF modules/attention.py:31-39 with
+// kernels/rope.py:12-28 and models/common.py:192-195), fp32 math, one
+// rounding.  The zero padding lets head dims the attention kernels do not
+// take (e.g. 72) run on the D = 128 kernels: padded dims add nothing to a
+// score, and the padded output columns are zero.  One warp per (token, head).
+__global__ void __launch_bounds__(256) vision_qkv_rope_kernel(
+    const uint16_t *__restrict__ qkv, const float *__restrict__ ang, uint16_t *__restrict__ q,
+    uint16_t *__restrict__ k, uint16_t *__restrict__ v, int64_t S, int H, int D, int Dp) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (wid >= S * H) return;
+  const int64_t s = wid / H;
+  const int h = static_cast<int>(wid % H);
+  const int half = D / 2;
+  const uint16_t *src = qkv + s * 3 * H * D;
+  const int64_t dst = (static_cast<int64_t>(h) * S + s) * Dp;
+  for (int j = lane; j < Dp; j += 32) {
+    float oq = 0.f, ok = 0.f, ov = 0.f;
+    if (j < D) {
+      const int j0 = j < half ? j : j - half;
+      float sn, cs;
+      sincosf(ang[s * half + j0], &sn, &cs);
+      const float q1 = bf2f(src[h * D + j0]), q2 = bf2f(src[h * D + j0 + half]);
+      const float k1 = bf2f(src[(H + h) * D + j0]), k2 = bf2f(src[(H + h) * D + j0 + half]);
+      if (j < half) {
+        oq = q1 * cs - q2 * sn;
+        ok = k1 * cs - k2 * sn;
+      } else {
+        oq = q2 * cs + q1 * sn;
+        ok = k2 * cs + k1 * sn;
+      }
+      ov = bf2f(src[(2 * H + h) * D + j]);
+    }
+    q[dst + j] = f2bf(oq);
+    k[dst + j] = f2bf(ok);
+    v[dst + j] = f2bf(ov);
+  }
+}
+
+// Token-major attention output [S, H, Dp] -> [S, H, D] (drops the padding).
+__global__ void __launch_bounds__(256) unpad_heads_kernel(const uint16_t *__restrict__ x,
+                                                          uint16_t *__restrict__ y, int64_t S,
+                                                          int H, int D, int Dp) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= S * H * D) return;
+  const int64_t sh = i / D;
+  const int d = static_cast<int>(i % D);
+  y[i] = x[sh * Dp + d];
+}
+
 }  // namespace
 }  // namespace q35
 
@@ -183,4 +236,34 @@ extern "C" int q35_conv3d_patch_fwd(const void *patches, const void *w, const vo
                                     q35_stream_t stream) {
   if (!patches || !w || !out) return fail(Q35_ERR_INVALID, "conv3d_patch: null pointer");
   return q35_gemm_bf16(patches, w, bias, nullptr, out, n_patches, embed, K, stream);
+}
+
+extern "C" int q35_vision_qkv_rope_pad(const void *qkv, const float *angles, void *q, void *k,
+                                       void *v, int64_t S, int H, int D, int Dp,
+                                       q35_stream_t stream) {
+  if (!qkv || !angles || !q || !k || !v) return fail(Q35_ERR_INVALID, "vision_qkv_rope: null");
+  if (S < 0 || H < 1 || D < 2 || D % 2 != 0 || Dp < D)
+    return fail(Q35_ERR_SHAPE, "vision_qkv_rope: S %lld H %d D %d (even) Dp %d (>= D)",
+                (long long)S, H, D, Dp);
+  if (S == 0) return Q35_OK;
+  const int64_t warps = S * H;
+  vision_qkv_rope_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0,
+                           reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t *>(qkv), angles, static_cast<uint16_t *>(q),
+      static_cast<uint16_t *>(k), static_cast<uint16_t *>(v), S, H, D, Dp);
+  Q35_LAUNCH_CHECK("vision_qkv_rope launch");
+  return Q35_OK;
+}
+
+extern "C" int q35_unpad_heads(const void *x, void *y, int64_t S, int H, int D, int Dp,
+                               q35_stream_t stream) {
+  if (!x || !y) return fail(Q35_ERR_INVALID, "unpad_heads: null");
+  if (S < 0 || H < 1 || D < 1 || Dp < D) return fail(Q35_ERR_SHAPE, "unpad_heads: bad shape");
+  const int64_t n = S * H * D;
+  if (n == 0) return Q35_OK;
+  unpad_heads_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0,
+                       reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t *>(x), static_cast<uint16_t *>(y), S, H, D, Dp);
+  Q35_LAUNCH_CHECK("unpad_heads launch");
+  return Q35_OK;
 }

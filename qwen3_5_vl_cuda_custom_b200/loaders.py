@@ -10,8 +10,10 @@ parameter names, which are the reference's own (REF loaders/hf.py:21-109):
   ``mlp.gate.weight`` -> ``mlp.gate_weight``;
 - the expert tensors are stored transposed on disk ((E, H, 2I) and (E, I, H));
   they are transposed on dims (1, 2) to (E, 2I, H) and (E, H, I);
-- ``model.visual.*`` (the vision tower) is not part of this library: those
-  keys are reported as ``skipped``, not loaded.
+- ``model.visual.<rest>`` -> ``visual.<rest>`` with ``patch_embed.proj.`` ->
+  ``patch_embed.``, ``pos_embed.weight`` -> ``pos_embed.emb.weight`` and
+  ``deepstack_merger_list.`` -> ``deepstack_mergers.``; a model built with
+  ``vision=False`` reports these keys as ``skipped``.
 
 Expert-parallel models (built with ``expert_group``) read only their own
 experts' rows from the files (``safe_open(...).get_slice``), so no rank
@@ -28,9 +30,14 @@ _EXPERT_KEYS = ("mlp.experts.gate_up_proj", "mlp.experts.down_proj")
 
 def map_hf_name(name: str) -> str | None:
     """Internal parameter name of an HF checkpoint key; None for keys this
-    library does not hold (the vision tower and anything unrecognised)."""
+    library does not hold."""
     if name == "lm_head.weight":
         return name
+    if name.startswith("model.visual."):
+        rest = name[len("model.visual."):].replace("patch_embed.proj.", "patch_embed.")
+        if rest == "pos_embed.weight":
+            rest = "pos_embed.emb.weight"
+        return "visual." + rest.replace("deepstack_merger_list.", "deepstack_mergers.")
     prefix = "model.language_model."
     if not name.startswith(prefix):
         return None
@@ -71,7 +78,7 @@ def load_hf_weights(model: torch.nn.Module, snapshot_path: str | Path) -> dict:
     for f in files:
         with safe_open(str(f), framework="pt", device="cpu") as sf:
             for key in sf.keys():
-                if key.startswith("model.visual."):
+                if key.startswith("model.visual.") and getattr(model, "visual", None) is None:
                     skipped.append(key)
                     continue
                 internal = map_hf_name(key)

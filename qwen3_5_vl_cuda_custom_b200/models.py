@@ -2,9 +2,11 @@
 
 ``CudaQwen3VLMoeModel(cfg).forward(input_ids, pixel_values, vision_position_ids,
 image_token_mask, position_ids, past_key_values, return_kv)`` returns
-``(logits, router_logits_list[, new_kvs])`` like the reference.  The vision
-tower is outside this library's scope: ``pixel_values`` must be None (callers
-with image features pass them through ``inputs_embeds``, an extra keyword).
+``(logits, router_logits_list[, new_kvs])`` like the reference.  With
+``pixel_values`` and ``image_token_mask`` the vision tower (``vision.py``; its
+grid (t, h, w) per image passed as ``vision_position_ids``, as in the
+reference) replaces the embeddings of the image tokens with its merged
+features.  ``vision=False`` builds a text-only model (``visual`` is None).
 """
 from __future__ import annotations
 
@@ -27,15 +29,20 @@ def _layer_uses_moe(cfg: MoETextConfig, layer_idx: int) -> bool:
 
 
 class CudaQwen3VLMoeModel(nn.Module):
-    def __init__(self, cfg: Qwen3VLConfig, expert_group=None) -> None:
+    def __init__(self, cfg: Qwen3VLConfig, expert_group=None, vision: bool = True) -> None:
         """``expert_group`` shards every MoE layer's experts over that process
-        group (expert parallelism); attention and the rest stay replicated."""
+        group (expert parallelism); attention and the rest stay replicated.
+        ``vision=False`` leaves the vision tower out (text-only use)."""
         super().__init__()
         if cfg.family != "moe" or not isinstance(cfg.text, MoETextConfig):
             raise ValueError(f"expected an MoE config, got {cfg.family}")
         self.cfg = cfg
         t = cfg.text
-        self.visual = None  # vision tower: not part of this library
+        if vision:
+            from .vision import CudaVisionTower
+            self.visual = CudaVisionTower(cfg.vision)
+        else:
+            self.visual = None
         self.embed_tokens = CudaEmbedding(t.vocab_size, t.hidden_size)
         self.rotary = TextMRoPE(t.head_dim, theta=t.rope_theta, mrope_section=t.mrope_section)
         self.layers = nn.ModuleList([
@@ -70,13 +77,18 @@ class CudaQwen3VLMoeModel(nn.Module):
     def forward(self, input_ids: torch.Tensor | None = None, pixel_values=None,
                 vision_position_ids=None, image_token_mask=None, position_ids=None,
                 past_key_values=None, return_kv: bool = False, inputs_embeds=None):
-        if pixel_values is not None:
-            raise NotImplementedError("the vision tower is not part of this library; "
-                                      "pass image features via inputs_embeds")
         if inputs_embeds is None:
             if input_ids is None:
                 raise ValueError("input_ids or inputs_embeds is required")
             inputs_embeds = self.embed_tokens(input_ids)
+        if pixel_values is not None and image_token_mask is not None:
+            # REF models/moe.py:87-90 (the reference unpacks two of the tower's
+            # three outputs there; the merged features are its first)
+            if self.visual is None:
+                raise RuntimeError("this model was built with vision=False")
+            feats = self.visual(pixel_values, vision_position_ids)[0]
+            inputs_embeds = inputs_embeds.clone()
+            inputs_embeds[image_token_mask] = feats.to(inputs_embeds.dtype)
         B, S = inputs_embeds.shape[:2]
         if position_ids is None:
             past_len = past_key_values[0][0].shape[2] if past_key_values else 0

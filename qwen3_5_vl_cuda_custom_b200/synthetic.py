@@ -118,3 +118,51 @@ def layer_flops(cfg: MoETextConfig, T: int, S: int) -> dict[str, float]:
     experts = T * k * (2.0 * H * 2 * I + 2.0 * I * H)
     return {"proj": proj, "attn": attn, "experts": experts, "total": proj + attn + experts,
             "router": 2.0 * T * H * cfg.num_experts}
+
+
+def vision_param_shapes(vc) -> list[tuple[str, tuple[int, ...]]]:
+    """Parameter names/shapes of CudaVisionTower (the reference's state-dict
+    layout, REF models/common.py:25-76), in registration order."""
+    C, I, O = vc.hidden_size, vc.intermediate_size, vc.out_hidden_size
+    M = C * vc.spatial_merge_size ** 2
+    out = [("patch_embed.weight", (C, vc.in_channels, vc.temporal_patch_size, vc.patch_size,
+                                   vc.patch_size)),
+           ("patch_embed.bias", (C,)),
+           ("pos_embed.emb.weight", (vc.num_position_embeddings, C))]
+    for i in range(vc.num_layers):
+        b = f"blocks.{i}."
+        out += [(b + "norm1.weight", (C,)), (b + "norm1.bias", (C,)),
+                (b + "attn.qkv.weight", (3 * C, C)), (b + "attn.qkv.bias", (3 * C,)),
+                (b + "attn.proj.weight", (C, C)), (b + "attn.proj.bias", (C,)),
+                (b + "norm2.weight", (C,)), (b + "norm2.bias", (C,)),
+                (b + "mlp.linear_fc1.weight", (I, C)), (b + "mlp.linear_fc1.bias", (I,)),
+                (b + "mlp.linear_fc2.weight", (C, I)), (b + "mlp.linear_fc2.bias", (C,))]
+    mergers = [("merger.", C)] + [(f"deepstack_mergers.{j}.", M)
+                                  for j in range(len(vc.deepstack_layers))]
+    for pre, nd in mergers:
+        out += [(pre + "norm.weight", (nd,)), (pre + "norm.bias", (nd,)),
+                (pre + "linear_fc1.weight", (M, M)), (pre + "linear_fc1.bias", (M,)),
+                (pre + "linear_fc2.weight", (O, M)), (pre + "linear_fc2.bias", (O,))]
+    return out
+
+
+def vision_params(vc, gen: torch.Generator) -> dict[str, torch.Tensor]:
+    """fp32 CPU state dict of a vision tower drawn from ``gen``: N(0, 0.02)
+    everywhere, LayerNorm weights 1 + N(0, 0.02); bf16-rounded (the GPU dtype)."""
+    out = {}
+    for name, shape in vision_param_shapes(vc):
+        t = torch.empty(shape, dtype=torch.float32).normal_(0.0, 0.02, generator=gen)
+        if "norm" in name and name.endswith(".weight"):
+            t += 1.0
+        out[name] = t.to(torch.bfloat16).float()
+    return out
+
+
+def tiny_vision_config():
+    """Small vision tower with the real head_dim (72 = 288 / 4): 3 blocks,
+    deepstack after blocks 0 and 2, an 8 x 8 position grid."""
+    from .configs import VisionConfig
+    return VisionConfig(hidden_size=288, num_layers=3, num_heads=4, intermediate_size=512,
+                        patch_size=16, temporal_patch_size=2, spatial_merge_size=2,
+                        in_channels=3, num_position_embeddings=64, out_hidden_size=256,
+                        rope_theta=10000.0, rms_norm_eps=1e-6, deepstack_layers=(0, 2))

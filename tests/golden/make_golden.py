@@ -80,6 +80,37 @@ def moe_module_case(seed: int = 5):
             "router_logits": logits}
 
 
+VISION_GRID = [[1, 8, 8], [2, 4, 4]]
+
+
+def vision_case(seed: int = 11) -> dict:
+    """The reference's CudaVisionTower (REF models/common.py:25-210) in fp32 on a
+    small config with the real head_dim 72, two images (one of two frames)."""
+    from cuda_qwen3_vl.configs import VisionConfig as RefVisionConfig
+    from cuda_qwen3_vl.models.common import CudaVisionTower
+    vc = syn.tiny_vision_config()
+    g = torch.Generator().manual_seed(seed)
+    P = syn.vision_params(vc, g)
+    grid = torch.tensor(VISION_GRID)
+    n = int(sum(t * h * w for t, h, w in VISION_GRID))
+    feat = vc.in_channels * vc.temporal_patch_size * vc.patch_size ** 2
+    x = syn.hidden_states((n, feat), g)
+    ref_cfg = RefVisionConfig(**{k: getattr(vc, k) for k in vc.__dataclass_fields__})
+    tower = CudaVisionTower(ref_cfg)
+    tower.load_state_dict(P)
+    with torch.no_grad():
+        pooled, last, deep = tower(x, grid)
+    return {"seed": seed, "grid_thw": VISION_GRID,
+            "input_checksum": checksum([x, *P.values()]),
+            "pooler_output": pooled.clone(), "last_hidden_state": last.clone(),
+            "deepstack": [d.clone() for d in deep]}
+
+
+def main_vision() -> None:
+    torch.save(vision_case(), OUT / "vision_reference.pt")
+    print("wrote", OUT / "vision_reference.pt")
+
+
 def main() -> None:
     cfg = tiny_moe_text()
     cases = {
@@ -91,7 +122,8 @@ def main() -> None:
     }
     torch.save(cases, OUT / "c1_reference.pt")
     print("wrote", OUT / "c1_reference.pt")
+    main_vision()
 
 
 if __name__ == "__main__":
-    main()
+    main_vision() if "--vision-only" in sys.argv else main()

@@ -104,7 +104,7 @@ def test_model_generate_matches_tuple_past_loop():
                       mrope_section=[16, 8, 8], num_experts=32, num_experts_per_tok=2,
                       moe_intermediate_size=64)
     torch.manual_seed(0)
-    model = CudaQwen3VLMoeModel(moe_config(t)).to(DEV, torch.bfloat16)
+    model = CudaQwen3VLMoeModel(moe_config(t), vision=False).to(DEV, torch.bfloat16)
     ids = torch.randint(0, 512, (2, 12), device=DEV)
     with torch.no_grad():
         out = model.generate(ids, max_new_tokens=5)

@@ -47,7 +47,7 @@ def test_text_model_logits_match_oracle_stack():
                       mrope_section=[8, 4, 4], num_experts=16, num_experts_per_tok=4,
                       moe_intermediate_size=128, mlp_only_layers=[1])
     torch.manual_seed(3)
-    model = CudaQwen3VLMoeModel(moe_config(t)).to(DEV, torch.bfloat16)
+    model = CudaQwen3VLMoeModel(moe_config(t), vision=False).to(DEV, torch.bfloat16)
     moe_layers = [_layer_uses_moe(t, i) for i in range(t.num_layers)]
     assert moe_layers == [True, False]
     ids = torch.randint(0, t.vocab_size, (2, 96), generator=torch.Generator().manual_seed(4))

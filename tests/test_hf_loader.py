@@ -40,7 +40,7 @@ def _write_checkpoint(path: Path, seed: int = 0) -> dict:
     from safetensors.torch import save_file
     from qwen3_5_vl_cuda_custom_b200.models import CudaQwen3VLMoeModel
     torch.manual_seed(seed)
-    src = CudaQwen3VLMoeModel(_tiny_cfg())
+    src = CudaQwen3VLMoeModel(_tiny_cfg(), vision=False)
     ref = {k: torch.randn_like(v) for k, v in src.state_dict().items()}
     hf = dict(_to_hf(k, v) for k, v in ref.items())
     hf["model.visual.blocks.0.norm1.weight"] = torch.ones(8)
@@ -55,7 +55,7 @@ def test_load_hf_checkpoint_round_trip(tmp_path):
     from qwen3_5_vl_cuda_custom_b200.loaders import load_hf_weights
     from qwen3_5_vl_cuda_custom_b200.models import CudaQwen3VLMoeModel
     ref = _write_checkpoint(tmp_path)
-    model = CudaQwen3VLMoeModel(_tiny_cfg())
+    model = CudaQwen3VLMoeModel(_tiny_cfg(), vision=False)
     report = load_hf_weights(model, tmp_path)
     assert report["missing"] == [] and report["mismatched"] == []
     assert report["unexpected"] == ["something.else"]
@@ -80,7 +80,7 @@ def test_name_mapping_matches_reference_loader():
         sys.path.remove(str(ref_dir))
     from qwen3_5_vl_cuda_custom_b200.loaders import map_hf_name
     from qwen3_5_vl_cuda_custom_b200.models import CudaQwen3VLMoeModel
-    model = CudaQwen3VLMoeModel(_tiny_cfg())
+    model = CudaQwen3VLMoeModel(_tiny_cfg(), vision=False)
     for name, t in model.state_dict().items():
         hf, _ = _to_hf(name, t)
         assert map_hf_name(hf) == ref_hf._map_name(hf) == name
@@ -101,7 +101,7 @@ def _ep_worker(rank, world, port, path, q):
         dist.init_process_group("gloo", rank=rank, world_size=world)
         from qwen3_5_vl_cuda_custom_b200.loaders import load_hf_weights
         from qwen3_5_vl_cuda_custom_b200.models import CudaQwen3VLMoeModel
-        model = CudaQwen3VLMoeModel(_tiny_cfg(), expert_group=dist.group.WORLD)
+        model = CudaQwen3VLMoeModel(_tiny_cfg(), expert_group=dist.group.WORLD, vision=False)
         report = load_hf_weights(model, path)
         ref = torch.load(Path(path) / "ref.pt")
         lo, hi = model.layers[0].mlp.exchange.expert_range
@@ -130,3 +130,25 @@ def test_expert_parallel_ranks_load_their_experts(tmp_path):
     for p in procs:
         p.join(timeout=60)
     assert all(v == "ok" for v in res.values()), res
+
+
+def test_vision_key_mapping_matches_reference():
+    """HF vision keys map onto the vision tower's parameter names by the
+    reference's rule (REF loaders/hf.py:41-52) and all exist in the tower."""
+    ref_dir = ROOT / "baseline" / "_ref"
+    if not (ref_dir / "cuda_qwen3_vl").exists():
+        pytest.skip("reference package not installed under baseline/_ref")
+    sys.path.insert(0, str(ref_dir))
+    os.environ.setdefault("CUDA_QWEN3_VL_AUTO_PRELOAD", "0")
+    from cuda_qwen3_vl.loaders import hf as ref_hf
+    from qwen3_5_vl_cuda_custom_b200 import synthetic as syn
+    from qwen3_5_vl_cuda_custom_b200.loaders import map_hf_name
+    from qwen3_5_vl_cuda_custom_b200.vision import CudaVisionTower
+    keys = ["model.visual.patch_embed.proj.weight", "model.visual.patch_embed.proj.bias",
+            "model.visual.pos_embed.weight", "model.visual.blocks.2.attn.qkv.bias",
+            "model.visual.blocks.0.mlp.linear_fc2.weight", "model.visual.merger.norm.weight",
+            "model.visual.deepstack_merger_list.1.linear_fc1.weight"]
+    names = set("visual." + k for k in CudaVisionTower(syn.tiny_vision_config()).state_dict())
+    for k in keys:
+        assert map_hf_name(k) == ref_hf._map_name(k)
+        assert map_hf_name(k) in names, k
