@@ -22,10 +22,11 @@
 //                             in this process (written once by the host)
 //
 // One call (one MoE layer forward):
-//   1. ep_dispatch_kernel: one warp per local token finds the ranks that own
-//      its experts; for each it reserves a row of that rank's slab
-//      (atomicAdd on a local counter) and stores the hidden row, the slot list,
-//      the weights and the token index into the peer's window.  The last CTA
+//   1. ep_dispatch_kernel: per CTA of 32 tokens, each token's owner ranks
+//      and its rank among the CTA's rows for each of them (shared-memory
+//      counters), one global atomicAdd per destination to reserve the CTA's
+//      block of that rank's slab, then the hidden rows, slot lists, weights
+//      and token indices stored into the peers' windows.  The last CTA
 //      to finish publishes the row counts and then the new epoch to every
 //      peer (release at system scope, after a system-scope fence).
 //   2. ep_wait_kernel: waits (bounded) until every source's dispatch flag has
@@ -134,50 +135,101 @@ __device__ void publish_when_last(uint32_t *ctrl, int done_word, bool bump_epoch
   ctrl[done_word] = 0u;
 }
 
-// One warp per token (grid-stride).  x [T, H] bf16, idx/w [T, k].
-// ret_pos [T, N]: d*Tcap + t where rank d returns token t's partial, else -1.
+constexpr int kTokPerCta = 32;  // dispatch: tokens per CTA (8 warps x 4)
+
+// Copies one row of H bf16 (H % 8 == 0) with the warp: up to 8 16-byte loads
+// per lane issued before their stores.
+__device__ __forceinline__ void warp_copy_row(uint4 *__restrict__ dst, const uint4 *__restrict__ src,
+                                              int64_t n16, int lane) {
+  for (int64_t c0 = 0; c0 < n16; c0 += 256) {
+    uint4 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t c = c0 + lane + 32 * i;
+      if (c < n16) v[i] = src[c];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int64_t c = c0 + lane + 32 * i;
+      if (c < n16) dst[c] = v[i];
+    }
+  }
+}
+
+// CTA = 32 consecutive tokens (warp w: tokens 4w..4w+3).  Pass 1 finds each
+// token's owner ranks and its rank among this CTA's rows for each destination
+// (shared-memory counters); one global atomicAdd per destination then reserves
+// the CTA's block of rows in that destination's slab; pass 2 stores the rows.
+// x [T, H] bf16, idx/w [T, k]; ret_pos [T, N]: d*Tcap + t where rank d returns
+// token t's partial, else -1.
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(
     const uint16_t *__restrict__ x, const int32_t *__restrict__ idx,
     const float *__restrict__ w, int64_t T, int k, int64_t H, int El, int N, int rank,
     int64_t Tcap, uint32_t *__restrict__ ctrl, const uint64_t *__restrict__ peers,
     DevLayout L, int32_t *__restrict__ ret_pos, int *err) {
-  const int lane = threadIdx.x & 31;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       t < T; t += warps) {
-    int e = -1, dst = -1;
+  __shared__ uint32_t s_used[kTokPerCta];
+  __shared__ int32_t s_rank[kTokPerCta][kMaxRanks];
+  __shared__ uint32_t s_cnt[kMaxRanks];
+  __shared__ int32_t s_base[kMaxRanks];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kTokPerCta;
+  if (threadIdx.x < kMaxRanks) s_cnt[threadIdx.x] = 0u;
+  __syncthreads();
+  // ---- pass 1: owner ranks and local ranks
+  for (int i = 0; i < kTokPerCta / 8; ++i) {
+    const int tl = warp * (kTokPerCta / 8) + i;
+    const int64_t t = t0 + tl;
+    uint32_t used = 0u;
+    if (t < T) {
+      int dst = -1;
+      if (lane < k) {
+        const int e = idx[t * k + lane];
+        if (e >= 0) {
+          dst = e / El;
+          if (dst >= N) {
+            report_error(err, DEV_ERR_INDEX, 301, static_cast<int>(t), e);
+            dst = -1;
+          }
+        }
+      }
+      used = __reduce_or_sync(0xffffffffu, dst >= 0 ? (1u << dst) : 0u);
+      if (lane < N) {
+        ret_pos[t * N + lane] = ((used >> lane) & 1u) ? static_cast<int32_t>(lane * Tcap + t) : -1;
+        if ((used >> lane) & 1u) s_rank[tl][lane] = static_cast<int32_t>(atomicAdd(&s_cnt[lane], 1u));
+      }
+    }
+    if (lane == 0) s_used[tl] = used;
+  }
+  __syncthreads();
+  if (threadIdx.x < N && s_cnt[threadIdx.x] > 0u)
+    s_base[threadIdx.x] = static_cast<int32_t>(atomicAdd(&ctrl[kCtrlSend + threadIdx.x], s_cnt[threadIdx.x]));
+  __syncthreads();
+  // ---- pass 2: rows, slot lists, weights and token ids into the owners' windows
+  for (int i = 0; i < kTokPerCta / 8; ++i) {
+    const int tl = warp * (kTokPerCta / 8) + i;
+    const int64_t t = t0 + tl;
+    if (t >= T) break;
+    int e = -1;
     float wt = 0.f;
     if (lane < k) {
       e = idx[t * k + lane];
       wt = w[t * k + lane];
-      if (e >= 0) {
-        dst = e / El;
-        if (dst >= N) {
-          report_error(err, DEV_ERR_INDEX, 301, static_cast<int>(t), e);
-          dst = -1;
-        }
-      }
     }
-    const uint32_t used = __reduce_or_sync(0xffffffffu, dst >= 0 ? (1u << dst) : 0u);
-    if (lane < N)
-      ret_pos[t * N + lane] = ((used >> lane) & 1u) ? static_cast<int32_t>(lane * Tcap + t) : -1;
     const uint4 *src = reinterpret_cast<const uint4 *>(x + t * H);
-    for (uint32_t m = used; m != 0u; m &= m - 1u) {
+    for (uint32_t m = s_used[tl]; m != 0u; m &= m - 1u) {
       const int d = __ffs(m) - 1;
-      int32_t p = 0;
-      if (lane == 0) p = static_cast<int32_t>(atomicAdd(&ctrl[kCtrlSend + d], 1u));
-      p = __shfl_sync(0xffffffffu, p, 0);
+      const int64_t p = static_cast<int64_t>(s_base[d]) + s_rank[tl][d];
       if (p >= Tcap) {  // cannot happen: at most one row per token and rank
-        if (lane == 0) report_error(err, DEV_ERR_INDEX, 302, static_cast<int>(t), p);
+        if (lane == 0) report_error(err, DEV_ERR_INDEX, 302, static_cast<int>(t), static_cast<int>(p));
         continue;
       }
       uint8_t *base = peer_base(peers, d);
       const int64_t row = static_cast<int64_t>(rank) * Tcap + p;
-      uint4 *drow = reinterpret_cast<uint4 *>(base + L.rows) + row * (H / 8);
-      for (int64_t c = lane; c < H / 8; c += 32) drow[c] = src[c];
+      warp_copy_row(reinterpret_cast<uint4 *>(base + L.rows) + row * (H / 8), src, H / 8, lane);
       if (lane < k) {
-        reinterpret_cast<int32_t *>(base + L.idx)[row * k + lane] = (dst == d) ? e - d * El : -1;
-        reinterpret_cast<float *>(base + L.wts)[row * k + lane] = (dst == d) ? wt : 0.f;
+        const bool mine = e >= 0 && e / El == d;
+        reinterpret_cast<int32_t *>(base + L.idx)[row * k + lane] = mine ? e - d * El : -1;
+        reinterpret_cast<float *>(base + L.wts)[row * k + lane] = mine ? wt : 0.f;
       }
       if (lane == 0) reinterpret_cast<int32_t *>(base + L.tok)[row] = static_cast<int32_t>(t);
     }
@@ -233,22 +285,63 @@ __global__ void __launch_bounds__(256) ep_return_kernel(
     const int32_t t = tok[r];
     uint4 *dst = reinterpret_cast<uint4 *>(peer_base(peers, s) + L.ret) +
                  (static_cast<int64_t>(rank) * Tcap + t) * (H / 8);
+    // the row's slots that hold an expert of this rank, compacted in slot
+    // order into registers of every lane (at most 8 are kept in registers;
+    // rows with more are summed by the general loop below)
+    int32_t pv[8];
+    float wv8[8];
+    int nv = 0;
+    bool spill = false;
+    for (int j = 0; j < k; ++j) {
+      const int32_t pj = __shfl_sync(0xffffffffu, sp, j);
+      const float wjj = __shfl_sync(0xffffffffu, wj, j);
+      if (pj < 0) continue;
+      if (nv < 8) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (q == nv) {
+            pv[q] = pj;
+            wv8[q] = wjj;
+          }
+        ++nv;
+      } else {
+        spill = true;
+      }
+    }
     for (int64_t c = lane; c < H / 8; c += 32) {
       float acc[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) acc[q] = 0.f;
-      for (int j = 0; j < k; ++j) {
-        const int32_t pj = __shfl_sync(0xffffffffu, sp, j);
-        const float wv = __shfl_sync(0xffffffffu, wj, j);
-        if (pj < 0) continue;
-        const uint4 u = reinterpret_cast<const uint4 *>(y + static_cast<int64_t>(pj) * H)[c];
-        float v[8];
-        unpack_bf2(u.x, v[0], v[1]);
-        unpack_bf2(u.y, v[2], v[3]);
-        unpack_bf2(u.z, v[4], v[5]);
-        unpack_bf2(u.w, v[6], v[7]);
+      if (!spill) {
+        uint4 u[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) acc[q] = fmaf(wv, v[q], acc[q]);
+        for (int j = 0; j < 8; ++j)
+          if (j < nv) u[j] = reinterpret_cast<const uint4 *>(y + static_cast<int64_t>(pv[j]) * H)[c];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (j >= nv) continue;
+          float v[8];
+          unpack_bf2(u[j].x, v[0], v[1]);
+          unpack_bf2(u[j].y, v[2], v[3]);
+          unpack_bf2(u[j].z, v[4], v[5]);
+          unpack_bf2(u[j].w, v[6], v[7]);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] = fmaf(wv8[j], v[q], acc[q]);
+        }
+      } else {
+        for (int j = 0; j < k; ++j) {
+          const int32_t pj = __shfl_sync(0xffffffffu, sp, j);
+          const float wjj = __shfl_sync(0xffffffffu, wj, j);
+          if (pj < 0) continue;
+          const uint4 uu = reinterpret_cast<const uint4 *>(y + static_cast<int64_t>(pj) * H)[c];
+          float v[8];
+          unpack_bf2(uu.x, v[0], v[1]);
+          unpack_bf2(uu.y, v[2], v[3]);
+          unpack_bf2(uu.z, v[4], v[5]);
+          unpack_bf2(uu.w, v[6], v[7]);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] = fmaf(wjj, v[q], acc[q]);
+        }
       }
       uint4 o;
       o.x = pack_bf2(acc[0], acc[1]);
@@ -381,7 +474,10 @@ extern "C" int q35_ep_dispatch(const void *x, const int32_t *idx, const float *w
   if (!err) return fail(Q35_ERR_CUDA, "ep_dispatch: no device error word");
   const Layout L = window_layout(N, Tcap, H, k);
   uint8_t *win = static_cast<uint8_t *>(window);
-  ep_dispatch_kernel<<<grid_for(T), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  // at least one CTA: a rank with no tokens still publishes its (empty) counts
+  const int64_t ctas = T > 0 ? (T + kTokPerCta - 1) / kTokPerCta : 1;
+  ep_dispatch_kernel<<<static_cast<unsigned>(ctas), 256, 0,
+                       reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t *>(x), idx, w, T, k, H, El, N, rank, Tcap,
       reinterpret_cast<uint32_t *>(win + L.ctrl), reinterpret_cast<const uint64_t *>(win + L.peers),
       dev_layout(L), ret_pos, err);
