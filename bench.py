@@ -204,20 +204,39 @@ def c4_embedding_input(w: Workload, dev) -> torch.Tensor:
     return x
 
 
-def build_layer(w: Workload, device, expert_group=None):
+def build_layer(w: Workload, device, expert_group=None, placement=None):
     from qwen3_5_vl_cuda_custom_b200.modules import CudaTextDecoderLayer, TextMRoPE
     cfg = w.cfg
     layer = CudaTextDecoderLayer(cfg.hidden_size, cfg.num_heads, cfg.num_kv_heads, cfg.head_dim,
                                  cfg.intermediate_size, cfg.rms_norm_eps, use_moe=True,
                                  num_experts=cfg.num_experts, top_k=cfg.num_experts_per_tok,
                                  moe_intermediate_size=cfg.moe_intermediate_size,
-                                 expert_group=expert_group)
+                                 expert_group=expert_group, expert_placement=placement)
     layer.load_state_dict(w.P)  # expert-parallel layers keep their slice of the experts
     layer = layer.to(device, torch.bfloat16)
     if w.bias is not None:
         layer.mlp.router_bias = w.bias.to(device, torch.float32)
     rot = TextMRoPE(cfg.head_dim, cfg.rope_theta, cfg.mrope_section).to(device)
     return layer, rot
+
+
+def calibrate_placement(w: Workload, x, pos, world: int):
+    """Balanced expert placement from a calibration routing of every rank's own
+    input: a single-GPU copy of the layer routes this rank's tokens, the
+    per-expert counts are summed over the ranks, and ``balanced_placement``
+    spreads the load (outside the timed region)."""
+    import torch.distributed as dist
+    from qwen3_5_vl_cuda_custom_b200.ep import balanced_placement
+    local, rot = build_layer(w, x.device, None)
+    H, E = w.cfg.hidden_size, w.cfg.num_experts
+    with torch.no_grad():
+        h = local.self_attn(local.input_layernorm(x), rot.bind(pos), residual=x,
+                            out_dtype=torch.float32)[0]
+        _, idx, _ = local.mlp.route(local.post_attention_layernorm(h).reshape(-1, H))
+        counts = torch.bincount(idx.reshape(-1).long(), minlength=E)
+    dist.all_reduce(counts)
+    del local
+    return balanced_placement(counts.cpu(), world), counts.cpu()
 
 
 def stage_table(cfg, T: int, S: int, world: int = 1) -> dict:
@@ -632,13 +651,24 @@ def run_ours(args, world, rank, local):
     if world > 1:
         import torch.distributed as dist
         ep_group = dist.group.WORLD
-    layer, rot = build_layer(w, dev, ep_group)
     x = c4_embedding_input(w, dev) if w.x_cpu is None else w.x_cpu.to(dev, torch.bfloat16)
     if w.x_cpu is None:
         w.x_cpu = x.float().cpu()
     B, S, _ = x.shape
     T = B * S
     pos = w.pos_cpu.to(dev)
+    placement, place_note = None, None
+    policy = args.placement if args.placement != "auto" else ("balanced" if w.bias is not None
+                                                               else "contiguous")
+    if world > 1 and policy == "balanced":
+        placement, counts = calibrate_placement(w, x, pos, world)
+        El = cfg.num_experts // world
+        loads = [int(counts[r * El:(r + 1) * El].sum()) for r in range(world)]
+        bal = [int(counts[torch.tensor(pl)].sum()) for pl in placement]
+        place_note = {"policy": "balanced from a calibration routing of the inputs",
+                      "max_over_mean_rows_contiguous": round(max(loads) * world / sum(loads), 3),
+                      "max_over_mean_rows_balanced": round(max(bal) * world / sum(bal), 3)}
+    layer, rot = build_layer(w, dev, ep_group, placement)
     flush = torch.empty(256 * 1024 * 1024 // 4, device=dev, dtype=torch.float32)
     bpos = rot.bind(pos)
     link_gbs = measure_link(world, rank, dev) if world > 1 else None
@@ -759,6 +789,7 @@ def run_ours(args, world, rank, local):
                                    f"dp{world} attention over sequences"
                                    if world > 1 else "1 GPU, all experts local"),
                    "router_skew": "0.5*log Zipf(1.2)" if w.bias is not None else None,
+                   "expert_placement": place_note or ("contiguous E/N blocks" if world > 1 else None),
                    "mode": mode,
                    "l2": "256 MiB flush between timed steps"},
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": in_bytes,
@@ -886,6 +917,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=None,
                     help="sequence length override (c2: 4096, c4/c5: 2048)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--placement", choices=["auto", "contiguous", "balanced"], default="auto",
+                    help="expert placement at N > 1 (auto: balanced when the router is skewed)")
     ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c2",
                     help="c2: the headline prefill layer (default); c4: 8x2048 strong scaling "
                          "with a skewed router; c5: multimodal 4x2048; c3: decode (one GPU)")

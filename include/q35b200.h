@@ -298,9 +298,13 @@ Q35_API int q35_ep_ipc_open(const void *handle64, void **peer_window);
 Q35_API int q35_ep_ipc_close(void *peer_window);
 Q35_API int q35_ep_set_peers(void *window, int N, int64_t Tcap, int64_t H, int k,
                              const uint64_t *peer_bases);
+/* expert_owner: NULL for the contiguous placement (expert e on rank e / El,
+ * local slot e % El), else int32 [N*El] in device memory: (rank << 16) | local
+ * slot of every expert (balanced placements).                               */
 Q35_API int q35_ep_dispatch(const void *x, const int32_t *idx, const float *w, int64_t T, int k,
-                            int64_t H, int El, int N, int rank, int64_t Tcap, void *window,
-                            int32_t *ret_pos, q35_stream_t stream);
+                            int64_t H, int El, int N, int rank, int64_t Tcap,
+                            const int32_t *expert_owner, void *window, int32_t *ret_pos,
+                            q35_stream_t stream);
 Q35_API int q35_ep_wait(void *window, int N, int64_t Tcap, int64_t H, int k, int which,
                         int64_t limit_ns, q35_stream_t stream);
 Q35_API int q35_ep_return(const void *y, const int32_t *slot_pos, int64_t Tcap, int k, int64_t H,

@@ -64,7 +64,7 @@ _SIGS = {
     "q35_ep_ipc_close": (c_int, [c_void_p]),
     "q35_ep_set_peers": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int, c_void_p]),
     "q35_ep_dispatch": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_int, c_int,
-                                c_int, c_int64, c_void_p, c_void_p, c_void_p]),
+                                c_int, c_int64, c_void_p, c_void_p, c_void_p, c_void_p]),
     "q35_ep_wait": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int, c_int, c_int64, c_void_p]),
     "q35_ep_return": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int64, c_int, c_int, c_void_p,
                               c_void_p]),

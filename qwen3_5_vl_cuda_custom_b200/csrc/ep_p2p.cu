@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
     const uint16_t *__restrict__ x, const int32_t *__restrict__ idx,
     const float *__restrict__ w, int64_t T, int k, int64_t H, int El, int N, int rank,
     int64_t Tcap, uint32_t *__restrict__ ctrl, const uint64_t *__restrict__ peers,
-    DevLayout L, int32_t *__restrict__ ret_pos, int *err) {
+    DevLayout L, int32_t *__restrict__ ret_pos, const int32_t *__restrict__ owner, int *err) {
   __shared__ uint32_t s_used[kTokPerCta];
   __shared__ int32_t s_rank[kTokPerCta][kMaxRanks];
   __shared__ uint32_t s_cnt[kMaxRanks];
@@ -184,12 +184,10 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
       int dst = -1;
       if (lane < k) {
         const int e = idx[t * k + lane];
-        if (e >= 0) {
-          dst = e / El;
-          if (dst >= N) {
-            report_error(err, DEV_ERR_INDEX, 301, static_cast<int>(t), e);
-            dst = -1;
-          }
+        if (e >= N * El) {
+          report_error(err, DEV_ERR_INDEX, 301, static_cast<int>(t), e);
+        } else if (e >= 0) {
+          dst = owner ? (owner[e] >> 16) : e / El;
         }
       }
       used = __reduce_or_sync(0xffffffffu, dst >= 0 ? (1u << dst) : 0u);
@@ -227,8 +225,13 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
       const int64_t row = static_cast<int64_t>(rank) * Tcap + p;
       warp_copy_row(reinterpret_cast<uint4 *>(base + L.rows) + row * (H / 8), src, H / 8, lane);
       if (lane < k) {
-        const bool mine = e >= 0 && e / El == d;
-        reinterpret_cast<int32_t *>(base + L.idx)[row * k + lane] = mine ? e - d * El : -1;
+        int dst_e = -1, local = -1;
+        if (e >= 0 && e < N * El) {
+          dst_e = owner ? (owner[e] >> 16) : e / El;
+          local = owner ? (owner[e] & 0xffff) : e - dst_e * El;
+        }
+        const bool mine = dst_e == d;
+        reinterpret_cast<int32_t *>(base + L.idx)[row * k + lane] = mine ? local : -1;
         reinterpret_cast<float *>(base + L.wts)[row * k + lane] = mine ? wt : 0.f;
       }
       if (lane == 0) reinterpret_cast<int32_t *>(base + L.tok)[row] = static_cast<int32_t>(t);
@@ -461,7 +464,8 @@ extern "C" int q35_ep_set_peers(void *window, int N, int64_t Tcap, int64_t H, in
 
 extern "C" int q35_ep_dispatch(const void *x, const int32_t *idx, const float *w, int64_t T,
                                int k, int64_t H, int El, int N, int rank, int64_t Tcap,
-                               void *window, int32_t *ret_pos, q35_stream_t stream) {
+                               const int32_t *expert_owner, void *window, int32_t *ret_pos,
+                               q35_stream_t stream) {
   if (!window || !ret_pos || (T > 0 && (!x || !idx || !w)))
     return fail(Q35_ERR_INVALID, "ep_dispatch: null pointer");
   int st = check_dims(N, Tcap, H, k);
@@ -480,7 +484,7 @@ extern "C" int q35_ep_dispatch(const void *x, const int32_t *idx, const float *w
                        reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t *>(x), idx, w, T, k, H, El, N, rank, Tcap,
       reinterpret_cast<uint32_t *>(win + L.ctrl), reinterpret_cast<const uint64_t *>(win + L.peers),
-      dev_layout(L), ret_pos, err);
+      dev_layout(L), ret_pos, expert_owner, err);
   Q35_LAUNCH_CHECK("ep_dispatch launch");
   return Q35_OK;
 }

@@ -194,6 +194,27 @@ class ExpertParallelExchange:
         return out
 
 
+def balanced_placement(counts, world: int) -> list[list[int]]:
+    """Experts per rank with equal numbers of experts (E/N) and near-equal
+    expected load: longest-processing-time assignment of the experts, heaviest
+    first, each to the least-loaded rank that still has room (ties to the lower
+    rank and expert id; deterministic).  ``counts`` [E]: tokens routed to each
+    expert on a calibration batch (all ranks' tokens)."""
+    c = [int(v) for v in (counts.tolist() if hasattr(counts, "tolist") else counts)]
+    E = len(c)
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    cap = E // world
+    order = sorted(range(E), key=lambda e: (-c[e], e))
+    load = [0] * world
+    out: list[list[int]] = [[] for _ in range(world)]
+    for e in order:
+        r = min((r for r in range(world) if len(out[r]) < cap), key=lambda r: (load[r], r))
+        out[r].append(e)
+        load[r] += c[e]
+    return [sorted(x) for x in out]
+
+
 def _default_transport(group) -> str:
     if dist.get_backend(group) != "nccl" or not torch.cuda.is_available():
         return "nccl"
@@ -206,8 +227,11 @@ class ExpertParallelSparseMoE(CudaSparseMoE):
     Same constructor arguments plus ``group``, ``transport`` ("p2p" or
     "nccl"; default p2p on NCCL groups, overridable with Q35_EP_TRANSPORT) and
     ``ep_max_tokens`` (tokens per rank the p2p window holds; default: the
-    first call's largest T over the ranks).  Same forward signature and
-    outputs.  The router weight is replicated; ``gate_up_proj`` and
+    first call's largest T over the ranks) and ``expert_placement`` (None: rank
+    r owns experts [r*E/N, (r+1)*E/N) as in a plain split; else N lists of E/N
+    global expert ids per rank, e.g. from ``balanced_placement``, so that a
+    skewed router does not load some ranks more than others; p2p transport).
+    Same forward signature and outputs.  The router weight is replicated; ``gate_up_proj`` and
     ``down_proj`` hold only this rank's E/N experts ([E/N, 2I, H], [E/N, H, I]).
     ``load_state_dict`` accepts the full-size expert tensors of a reference
     state dict and keeps this rank's slice, so the reference's weight names and
@@ -218,26 +242,53 @@ class ExpertParallelSparseMoE(CudaSparseMoE):
 
     def __init__(self, hidden_size: int, moe_intermediate_size: int, num_experts: int, top_k: int,
                  norm_topk_prob: bool = True, group=None, transport: str | None = None,
-                 ep_max_tokens: int | None = None):
+                 ep_max_tokens: int | None = None, expert_placement=None):
         super().__init__(hidden_size, moe_intermediate_size, num_experts, top_k, norm_topk_prob)
         self.exchange = ExpertParallelExchange(num_experts, group)
         self.transport = transport or _default_transport(group)
         if self.transport not in ("p2p", "nccl"):
             raise ValueError(f"unknown expert-parallel transport {self.transport!r}")
         self.ep_max_tokens = ep_max_tokens
-        lo, hi = self.exchange.expert_range
+        N, El, rank = self.exchange.world, self.exchange.E_local, self.exchange.rank
+        if expert_placement is None:
+            self.local_experts = list(range(rank * El, (rank + 1) * El))
+            self._owner_cpu = None
+        else:
+            pl = [list(map(int, x)) for x in expert_placement]
+            if len(pl) != N or sorted(e for x in pl for e in x) != list(range(num_experts)) \
+                    or any(len(x) != El for x in pl):
+                raise ValueError("expert_placement: N lists of E/N distinct expert ids covering all experts")
+            if self.transport != "p2p":
+                raise ValueError("expert_placement needs the p2p transport")
+            self.local_experts = pl[rank]
+            owner = torch.empty(num_experts, dtype=torch.int32)
+            for r, x in enumerate(pl):
+                for j, e in enumerate(x):
+                    owner[e] = (r << 16) | j
+            self._owner_cpu = owner
+        self.expert_placement = expert_placement
+        self._owner = None
+        sel = torch.tensor(self.local_experts)
         with torch.no_grad():
-            self.gate_up_proj = torch.nn.Parameter(self.gate_up_proj[lo:hi].clone())
-            self.down_proj = torch.nn.Parameter(self.down_proj[lo:hi].clone())
+            self.gate_up_proj = torch.nn.Parameter(self.gate_up_proj[sel].clone())
+            self.down_proj = torch.nn.Parameter(self.down_proj[sel].clone())
         self._ones = None
 
+    def _owner_table(self, device):
+        """Device table (rank << 16 | local slot) per expert, or None (plain split)."""
+        if self._owner_cpu is None:
+            return None
+        if self._owner is None or self._owner.device != device:
+            self._owner = self._owner_cpu.to(device)
+        return self._owner
+
     def _load_from_state_dict(self, state_dict, prefix, *args, **kwargs):
-        lo, hi = self.exchange.expert_range
+        sel = torch.tensor(self.local_experts)
         for name in ("gate_up_proj", "down_proj"):
             key = prefix + name
             t = state_dict.get(key)
-            if t is not None and t.shape[0] == self.num_experts and hi - lo != self.num_experts:
-                state_dict[key] = t[lo:hi]
+            if t is not None and t.shape[0] == self.num_experts and len(sel) != self.num_experts:
+                state_dict[key] = t[sel.to(t.device)]
         super()._load_from_state_dict(state_dict, prefix, *args, **kwargs)
 
     # ------------------------------------------------------------ p2p transport
@@ -266,9 +317,11 @@ class ExpertParallelSparseMoE(CudaSparseMoE):
             win = _window_for(ex.group, dev, N, rank, T, H, k, self.ep_max_tokens)
             stream = torch.cuda.current_stream(dev).cuda_stream
             ret_pos = torch.empty(T, N, device=dev, dtype=torch.int32)
+            owner = self._owner_table(dev)
             with torch.cuda.device(dev):
                 _lib.call("q35_ep_dispatch", x2d.data_ptr(), idx.data_ptr(), w.data_ptr(), T, k, H,
-                          El, N, rank, win.Tcap, win.ptr, ret_pos.data_ptr(), stream)
+                          El, N, rank, win.Tcap, None if owner is None else owner.data_ptr(),
+                          win.ptr, ret_pos.data_ptr(), stream)
                 _lib.call("q35_ep_wait", win.ptr, N, win.Tcap, H, k, 0, WAIT_LIMIT_NS, stream)
             st["win"], st["ret_pos"] = win, ret_pos
 

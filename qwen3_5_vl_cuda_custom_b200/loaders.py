@@ -57,7 +57,9 @@ def _expert_range(model: torch.nn.Module, internal: str) -> tuple[int, int] | No
     except AttributeError:
         return None
     ex = getattr(mod, "exchange", None)
-    return ex.expert_range if ex is not None else None
+    if ex is None or getattr(mod, "expert_placement", None) is not None:
+        return None  # all experts (a placed layer selects its own rows on load)
+    return ex.expert_range
 
 
 def load_hf_weights(model: torch.nn.Module, snapshot_path: str | Path) -> dict:
@@ -95,6 +97,9 @@ def load_hf_weights(model: torch.nn.Module, snapshot_path: str | Path) -> dict:
                     tensor = sf.get_tensor(key)
                 if is_expert:
                     tensor = tensor.transpose(1, 2)
+                    mod = model.get_submodule(internal.rsplit(".", 1)[0])
+                    if rng is None and getattr(mod, "expert_placement", None) is not None:
+                        tensor = tensor[torch.tensor(mod.local_experts)]
                 if tuple(tensor.shape) != tuple(target.shape):
                     mismatched.append((key, tuple(tensor.shape), tuple(target.shape)))
                     continue

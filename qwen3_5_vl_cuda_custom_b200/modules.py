@@ -412,9 +412,10 @@ class CudaTextDecoderLayer(nn.Module):
     def __init__(self, hidden_size: int, num_heads: int, num_kv_heads: int, head_dim: int,
                  intermediate_size: int, rms_norm_eps: float, use_moe: bool = False,
                  num_experts: int = 0, top_k: int = 0, moe_intermediate_size: int = 0,
-                 attention_bias: bool = False, expert_group=None) -> None:
+                 attention_bias: bool = False, expert_group=None, expert_placement=None) -> None:
         """``expert_group`` (a torch.distributed process group, optional) shards
-        the MoE experts over its ranks (expert parallelism, see ep.py)."""
+        the MoE experts over its ranks (expert parallelism, see ep.py);
+        ``expert_placement`` (optional) says which experts each rank owns."""
         super().__init__()
         self.input_layernorm = CudaRMSNorm(hidden_size, eps=rms_norm_eps)
         self.self_attn = CudaFullAttention(hidden_size=hidden_size, num_heads=num_heads,
@@ -424,7 +425,7 @@ class CudaTextDecoderLayer(nn.Module):
         if use_moe and expert_group is not None:
             from .ep import ExpertParallelSparseMoE
             self.mlp = ExpertParallelSparseMoE(hidden_size, moe_intermediate_size, num_experts, top_k,
-                                               group=expert_group)
+                                               group=expert_group, expert_placement=expert_placement)
         elif use_moe:
             self.mlp = CudaSparseMoE(hidden_size=hidden_size, moe_intermediate_size=moe_intermediate_size,
                                      num_experts=num_experts, top_k=top_k)

@@ -83,7 +83,7 @@ def test_ep_window_layout(lib):
 def test_ep_and_selftest_validation(lib):
     p = ctypes.c_void_p(256)  # never dereferenced: validation fails first
     # T above the window's capacity
-    assert lib.q35_ep_dispatch(p, p, p, 5000, 8, 2048, 16, 8, 0, 4096, p, p, None) == 2
+    assert lib.q35_ep_dispatch(p, p, p, 5000, 8, 2048, 16, 8, 0, 4096, None, p, p, None) == 2
     assert lib.q35_ep_wait(p, 8, 4096, 2048, 8, 2, 1000, None) == 1  # which
     assert lib.q35_ep_wait(p, 8, 4096, 2048, 8, 0, 0, None) == 1  # limit
     assert lib.q35_selftest_wait_timeout(0, None) == 1

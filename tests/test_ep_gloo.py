@@ -123,3 +123,22 @@ def test_rank_failure_is_reported_not_hung():
         if p.is_alive():
             p.kill()
     assert rank == 0 and msg.startswith("error"), msg
+
+
+def test_balanced_placement_spreads_skewed_load():
+    """Longest-processing-time placement: E/N experts per rank, every expert
+    once, the busiest rank within one expert's load of the mean on a
+    Zipf-skewed count vector, never worse than the contiguous split."""
+    from qwen3_5_vl_cuda_custom_b200.ep import balanced_placement
+    E, N = 128, 8
+    rng = np.random.default_rng(3)
+    pop = 1.0 / np.arange(1, E + 1) ** 1.2
+    counts = (pop[rng.permutation(E)] * 1e6).astype(np.int64)
+    pl = balanced_placement(counts, N)
+    assert sorted(e for r in pl for e in r) == list(range(E))
+    assert all(len(r) == E // N for r in pl)
+    loads = [int(counts[r].sum()) for r in pl]
+    contiguous = [int(counts[i * 16:(i + 1) * 16].sum()) for i in range(N)]
+    assert max(loads) - np.mean(loads) <= counts.max()
+    assert max(loads) <= max(contiguous)
+    assert balanced_placement(counts, N) == pl  # deterministic

@@ -51,7 +51,7 @@ def test_exchange_return_wait_gives_up_and_reports():
         w = torch.full((4, k), 0.5, device="cuda")
         ret_pos = torch.empty(4, N, device="cuda", dtype=torch.int32)
         _lib.call("q35_ep_dispatch", x.data_ptr(), idx.data_ptr(), w.data_ptr(), 4, k, H, El, N, 0,
-                  Tcap, p.value, ret_pos.data_ptr(), stream)
+                  Tcap, None, p.value, ret_pos.data_ptr(), stream)
         _lib.call("q35_ep_wait", p.value, N, Tcap, H, k, 0, 1_000_000_000, stream)
         K.device_error_check()  # the rows arrived: no error
         assert ret_pos.cpu().flatten().tolist() == [0, 1, 2, 3]
