@@ -316,6 +316,13 @@ Q35_API int q35_ep_return(const void *y, const int32_t *slot_pos, int64_t Tcap, 
  * microseconds waited) in the device error word and returns.               */
 Q35_API int q35_selftest_wait_timeout(int64_t limit_ns, q35_stream_t stream);
 
+/* Token embedding: out[r,:] = table[ids[r],:] for int64 ids (bf16 [V, cols],
+ * cols % 8 == 0).  Replaces embedding_forward (REF csrc/embedding_op.cu:5-97,
+ * kernels/embedding.py).  Ids are checked on the device: an id outside [0, V)
+ * gives a zero row and DEV_ERR_INDEX (site 104) in the device error word.    */
+Q35_API int q35_embedding_fwd(const void *table, const int64_t *ids, void *out, int64_t n,
+                              int64_t V, int64_t cols, q35_stream_t stream);
+
 /* dst[r,:] = src[rows[r],:] for r < n (bf16, cols % 8 == 0); n may be read
  * from device memory (n_dev != NULL: *n_dev rows, at most n_max).           */
 Q35_API int q35_gather_rows(const void *src, const int32_t *rows, void *dst,

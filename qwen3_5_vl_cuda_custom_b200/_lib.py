@@ -23,6 +23,7 @@ _SIGS = {
     "q35_version": (c_char_p, []),
     "q35_set_sm_limit": (c_int, [c_int]),
     "q35_launch_count": (c_int64, []),
+    "q35_embedding_fwd": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
     "q35_vision_qkv_rope_pad": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64,
                                         c_int, c_int, c_int, c_void_p]),
     "q35_unpad_heads": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p]),

@@ -365,6 +365,47 @@ extern "C" int q35_moe_permute_slabs(const int32_t *idx, int n_slabs,
                       slot_pos, tile_offsets, workspace, slab_cnt, slab_rows, stream);
 }
 
+namespace q35 {
+namespace {
+// out[r,:] = table[ids[r],:]; one warp per row, 16-byte vectors; an id outside
+// [0, V) writes a zero row and reports DEV_ERR_INDEX (site 104).
+__global__ void __launch_bounds__(256) embedding_kernel(const uint16_t *__restrict__ table,
+                                                        const int64_t *__restrict__ ids,
+                                                        uint16_t *__restrict__ out, int64_t n,
+                                                        int64_t V, int64_t cols, int *err) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (r >= n) return;
+  const int64_t id = ids[r];
+  uint4 *dp = reinterpret_cast<uint4 *>(out + r * cols);
+  if (id < 0 || id >= V) {
+    if (lane == 0) report_error(err, DEV_ERR_INDEX, 104, static_cast<int>(r), static_cast<int>(id));
+    for (int64_t c = lane; c < cols / 8; c += 32) dp[c] = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  const uint4 *sp = reinterpret_cast<const uint4 *>(table + id * cols);
+  for (int64_t c = lane; c < cols / 8; c += 32) dp[c] = sp[c];
+}
+}  // namespace
+}  // namespace q35
+
+extern "C" int q35_embedding_fwd(const void *table, const int64_t *ids, void *out, int64_t n,
+                                 int64_t V, int64_t cols, q35_stream_t stream) {
+  if (!table || !out || (n > 0 && !ids)) return fail(Q35_ERR_INVALID, "embedding: null pointer");
+  if (n < 0 || V < 1 || cols <= 0 || cols % 8 != 0)
+    return fail(Q35_ERR_SHAPE, "embedding: n %lld V %lld cols %lld (x8)", (long long)n,
+                (long long)V, (long long)cols);
+  if (!aligned16(table) || !aligned16(out)) return fail(Q35_ERR_ALIGN, "embedding: alignment");
+  if (n == 0) return Q35_OK;
+  int *err = device_error_word();
+  if (!err) return fail(Q35_ERR_CUDA, "embedding: no device error word");
+  embedding_kernel<<<static_cast<unsigned>((n + 7) / 8), 256, 0,
+                     reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t *>(table), ids, static_cast<uint16_t *>(out), n, V, cols, err);
+  Q35_LAUNCH_CHECK("embedding launch");
+  return Q35_OK;
+}
+
 extern "C" int q35_gather_rows(const void *src, const int32_t *rows, void *dst,
                                int64_t n_max, const int32_t *n_dev,
                                int64_t cols, q35_stream_t stream) {

@@ -338,6 +338,24 @@ def gather_rows(src: torch.Tensor, rows: torch.Tensor, n_dev: torch.Tensor | Non
     return dst
 
 
+def embedding(ids: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """weight[ids] for int32/int64 ids of any shape (REF kernels/embedding.py),
+    ids checked on the device: out-of-range ids give zero rows and a device
+    error report instead of a read outside the table."""
+    w = _require(weight, "embedding.weight")
+    if ids.device != w.device:
+        raise RuntimeError("embedding: ids and weight on different devices")
+    flat = ids.reshape(-1)
+    flat = flat if flat.dtype == torch.int64 else flat.to(torch.int64)
+    flat = flat.contiguous()
+    V, C = w.shape
+    out = torch.empty(flat.numel(), C, device=w.device, dtype=w.dtype)
+    with torch.cuda.device(w.device):
+        _lib.call("q35_embedding_fwd", w.data_ptr(), flat.data_ptr(), out.data_ptr(), flat.numel(),
+                  V, C, _stream(w))
+    return out.reshape(*ids.shape, C)
+
+
 def pack_b_tiles(w: torch.Tensor) -> torch.Tensor:
     """Copy of a bf16 weight [..., rows, K] as contiguous 128 x 64 tiles (the
     layout the grouped GEMMs stream with one 16 KB read per TMA box)."""
@@ -617,7 +635,7 @@ def device_error_check():
 
 __all__ = [
     "rmsnorm", "matmul", "softmax", "cuda_topk", "cuda_index_add", "swiglu", "residual_add",
-    "router_topk", "router_split_weights", "pack_b_tiles", "moe_permute", "moe_permute_slabs", "moe_permute_counted", "router_fused_supported", "Permutation", "gather_rows", "grouped_gateup_swiglu",
+    "router_topk", "router_split_weights", "pack_b_tiles", "embedding", "moe_permute", "moe_permute_slabs", "moe_permute_counted", "router_fused_supported", "Permutation", "gather_rows", "grouped_gateup_swiglu",
     "grouped_down", "moe_combine", "qknorm_mrope", "mrope", "attention_tokens",
     "flash_attention", "attention_cache", "kv_append", "device_error_check", "default_scale",
     "layernorm", "gelu_tanh", "apply_rope", "conv3d_patch",

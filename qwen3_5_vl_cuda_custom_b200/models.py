@@ -108,6 +108,18 @@ class CudaQwen3VLMoeModel(nn.Module):
         device = device or self.embed_tokens.weight.device
         return KVCache(len(self.layers), batch, t.num_kv_heads, capacity, t.head_dim, device)
 
+    def _last_logits(self, input_ids: torch.Tensor, cache) -> torch.Tensor:
+        """Logits of the last position only (B, vocab): the forward of
+        ``forward(input_ids, past_key_values=cache)`` with the lm_head applied to
+        the last hidden row instead of all of them."""
+        B, S = input_ids.shape
+        emb = self.embed_tokens(input_ids)
+        past_len = cache.length if cache is not None else 0
+        pos = torch.arange(past_len, past_len + S, device=emb.device).unsqueeze(0).expand(B, S)
+        hidden, _, _ = self._text_forward(emb, torch.stack([pos, pos, pos], dim=0),
+                                          past_key_values=cache)
+        return self.lm_head(hidden[:, -1:].contiguous())[:, 0]
+
     @torch.no_grad()
     def generate(self, input_ids: torch.Tensor, max_new_tokens: int, eos_token_id: int | None = None,
                  kv_cache: KVCache | None = None) -> torch.Tensor:
@@ -125,15 +137,13 @@ class CudaQwen3VLMoeModel(nn.Module):
                                                                          input_ids.device)
         if cache.length + S + max_new_tokens - 1 > cache[0].capacity:
             raise RuntimeError("generate: the KV cache is too small for the requested tokens")
-        logits, _ = self.forward(input_ids, past_key_values=cache)
-        nxt = logits[:, -1].argmax(dim=-1)
+        nxt = self._last_logits(input_ids, cache).argmax(dim=-1)
         out = [nxt]
         done = (nxt == eos_token_id) if eos_token_id is not None else None
         for _ in range(max_new_tokens - 1):
             if done is not None and bool(done.all()):
                 break
-            logits, _ = self.forward(nxt[:, None], past_key_values=cache)
-            nxt = logits[:, -1].argmax(dim=-1)
+            nxt = self._last_logits(nxt[:, None], cache).argmax(dim=-1)
             if done is not None:
                 nxt = torch.where(done, torch.full_like(nxt, eos_token_id), nxt)
                 done = done | (nxt == eos_token_id)

@@ -93,11 +93,11 @@ class CudaEmbedding(nn.Module):
                 self.weight[self.padding_idx].zero_()
 
     def forward(self, ids: torch.Tensor) -> torch.Tensor:
-        if ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= self.num_embeddings):
-            raise IndexError("CudaEmbedding: token id out of range")
-        rows = ids.reshape(-1).to(torch.int32)
-        out = K.gather_rows(self.weight, rows)
-        return out.reshape(*ids.shape, self.embedding_dim)
+        """Row gather with the id range checked on the device (no host
+        synchronisation): an id outside [0, num_embeddings) yields a zero row and
+        is reported through the device error word (``kernels.device_error_check``)."""
+        out = K.embedding(ids, self.weight)
+        return out
 
 
 # ------------------------------------------------------------------ rotary

@@ -60,3 +60,23 @@ def test_exchange_return_wait_gives_up_and_reports():
     finally:
         torch.cuda.synchronize()
         _lib.call("q35_ep_window_free", p.value)
+
+
+def test_embedding_matches_table_and_reports_bad_ids():
+    """The token embedding is an exact row copy (REF kernels/embedding.py); an
+    id outside [0, V) gives a zero row and records DEV_ERR_INDEX (code 2,
+    site 104) instead of reading outside the table, with no host sync."""
+    V, C = 1000, 2048
+    w = torch.randn(V, C, device="cuda").bfloat16()
+    ids = torch.randint(0, V, (3, 37), device="cuda")
+    got = K.embedding(ids, w)
+    assert got.shape == (3, 37, C) and torch.equal(got, w[ids])
+    assert torch.equal(K.embedding(ids.int(), w), w[ids])
+    K.device_error_check()
+    bad = torch.tensor([5, V, -1, 7], device="cuda")
+    out = K.embedding(bad, w)
+    with pytest.raises(RuntimeError, match="device error code 2 at site 104"):
+        K.device_error_check()
+    K.device_error_check()
+    assert torch.equal(out[0], w[5]) and torch.equal(out[3], w[7])
+    assert not out[1].any() and not out[2].any()
