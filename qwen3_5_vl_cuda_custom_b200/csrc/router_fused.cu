@@ -302,17 +302,45 @@ __global__ void __launch_bounds__(kPThreads) permute_scan_scatter_kernel(
   int32_t *s_off = psm + E;        // [E] expert offsets
   int32_t *s_tot = psm + 2 * E;    // [E] expert totals
   uint32_t(*mask)[4] = reinterpret_cast<uint32_t(*)[4]>(psm + 3 * E);
+  int32_t *s_ids = psm + 7 * E;    // [kPChunk * k] this chunk's expert ids
   const int64_t c = blockIdx.x;
+  // The chunk's ids first, as one coalesced sweep: the loads are all in
+  // flight together and overlap the chunk-count reads below.
+  const int64_t t_lo = c * kPChunk;
+  const int n_ids = static_cast<int>(T - t_lo < kPChunk ? T - t_lo : kPChunk) * k;
+  const int32_t *ids_g = idx + t_lo * k;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < n_ids; i += kPThreads) s_ids[i] = __ldg(ids_g + i);
   for (int e = threadIdx.x; e < E; e += kPThreads) {
-    int32_t before = 0, after = 0;
-#pragma unroll 8
-    for (int64_t cc = 0; cc < c; ++cc) before += chunk_counts[cc * E + e];
-#pragma unroll 8
-    for (int64_t cc = c; cc < n_chunks; ++cc) after += chunk_counts[cc * E + e];
-    s_base[e] = before;
-    s_tot[e] = before + after;
+    s_base[e] = 0;
+    s_tot[e] = 0;
   }
   for (int i = threadIdx.x; i < E * 4; i += kPThreads) mask[i >> 2][i & 3] = 0u;
+  __syncthreads();
+  // Chunk bases and expert totals: one coalesced sweep over all chunk counts
+  // by the whole CTA (independent loads, a few in flight per thread), summed
+  // with shared-memory atomics -- no per-expert serial walk over the chunks.
+  {
+    const int n_all = static_cast<int>(n_chunks) * E;
+    const int split = static_cast<int>(c) * E;  // entries of the chunks before this one
+    for (int i0 = threadIdx.x; i0 < n_all; i0 += 8 * kPThreads) {
+      int32_t v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = i0 + u * kPThreads;
+        v[u] = i < n_all ? __ldg(chunk_counts + i) : 0;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (v[u] != 0) {
+          const int i = i0 + u * kPThreads;
+          const int e = i % E;
+          atomicAdd(&s_tot[e], v[u]);
+          if (i < split) atomicAdd(&s_base[e], v[u]);
+        }
+      }
+    }
+  }
   __syncthreads();
   if (threadIdx.x < 32) {
     // exclusive scans over experts: lane l owns a contiguous run of experts
@@ -351,11 +379,12 @@ __global__ void __launch_bounds__(kPThreads) permute_scan_scatter_kernel(
     }
   }
   // this chunk's token masks
-  const int64_t t = c * kPChunk + threadIdx.x;
+  const int64_t t = t_lo + threadIdx.x;
   const bool mine = threadIdx.x < kPChunk && t < T;
+  const int32_t *my_ids = s_ids + threadIdx.x * k;
   if (mine) {
     for (int j = 0; j < k; ++j) {
-      const int e = idx[t * k + j];
+      const int e = my_ids[j];
       if (e < 0) continue;
       if (e >= E) {
         report_error(err, DEV_ERR_INDEX, 411, static_cast<int>(t), e);
@@ -365,21 +394,27 @@ __global__ void __launch_bounds__(kPThreads) permute_scan_scatter_kernel(
     }
   }
   __syncthreads();
-  if (!mine) return;
-  const int w = threadIdx.x >> 5, b = threadIdx.x & 31;
-  for (int j = 0; j < k; ++j) {
-    const int e = idx[t * k + j];
-    if (e < 0 || e >= E) {
-      slot_pos[t * k + j] = -1;
-      continue;
+  if (mine) {
+    // each thread overwrites only its own ids with their slot positions
+    int32_t *my_pos = s_ids + threadIdx.x * k;
+    const int w = threadIdx.x >> 5, b = threadIdx.x & 31;
+    for (int j = 0; j < k; ++j) {
+      const int e = my_pos[j];
+      if (e < 0 || e >= E) {
+        my_pos[j] = -1;
+        continue;
+      }
+      int rank = 0;
+      for (int qq = 0; qq < w; ++qq) rank += __popc(mask[e][qq]);
+      rank += __popc(mask[e][w] & ((1u << b) - 1u));
+      const int32_t pos = s_off[e] + s_base[e] + rank;
+      sorted_tok[pos] = static_cast<int32_t>(t);
+      my_pos[j] = pos;
     }
-    int rank = 0;
-    for (int qq = 0; qq < w; ++qq) rank += __popc(mask[e][qq]);
-    rank += __popc(mask[e][w] & ((1u << b) - 1u));
-    const int32_t pos = s_off[e] + s_base[e] + rank;
-    sorted_tok[pos] = static_cast<int32_t>(t);
-    slot_pos[t * k + j] = pos;
   }
+  __syncthreads();
+  int32_t *pos_g = slot_pos + t_lo * k;
+  for (int i = threadIdx.x; i < n_ids; i += kPThreads) pos_g[i] = s_ids[i];
 }
 
 template <int E>
@@ -465,15 +500,17 @@ extern "C" int q35_moe_permute_counted(const int32_t *idx, int64_t T, int k, int
   if (!chunk_counts || !counts || !offsets || !tile_offsets ||
       (T > 0 && (!idx || !sorted_tok || !slot_pos)))
     return fail(Q35_ERR_INVALID, "moe_permute_counted: null pointer");
-  if (T < 0 || k < 1 || E < 1 || E > 1024)
-    return fail(Q35_ERR_SHAPE, "moe_permute_counted: T %lld k %d E %d (E <= 1024)",
+  if (T < 0 || k < 1 || k > 16 || E < 1 || E > 1024)
+    return fail(Q35_ERR_SHAPE, "moe_permute_counted: T %lld k %d E %d (k <= 16, E <= 1024)",
                 (long long)T, k, E);
   if (T * k >= (int64_t(1) << 31))
     return fail(Q35_ERR_SHAPE, "moe_permute_counted: T*k exceeds int32");
   int *err = device_error_word();
   if (!err) return fail(Q35_ERR_CUDA, "moe_permute_counted: no device error word");
   const int64_t chunks = (T + kPChunk - 1) / kPChunk;
-  const size_t smem = static_cast<size_t>(E) * (3 * 4 + 16);
+  if (chunks * E >= (int64_t(1) << 31))
+    return fail(Q35_ERR_SHAPE, "moe_permute_counted: chunk counts exceed int32");
+  const size_t smem = static_cast<size_t>(E) * (3 * 4 + 16) + static_cast<size_t>(kPChunk) * k * 4;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // T == 0: one CTA over no rows writes zero counts and offsets
   permute_scan_scatter_kernel<<<static_cast<unsigned>(chunks > 0 ? chunks : 1), kPThreads, smem,
