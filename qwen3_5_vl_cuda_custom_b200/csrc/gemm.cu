@@ -835,6 +835,7 @@ int launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmPar
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   Q35_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, ta, tb, tb64 ? *tb64 : tb, p));
+  count_launch();
   return Q35_OK;
 }
 
