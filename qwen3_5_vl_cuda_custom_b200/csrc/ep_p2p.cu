@@ -135,7 +135,9 @@ __device__ void publish_when_last(uint32_t *ctrl, int done_word, bool bump_epoch
   ctrl[done_word] = 0u;
 }
 
-constexpr int kTokPerCta = 32;  // dispatch: tokens per CTA (8 warps x 4)
+// dispatch: tokens per CTA.  32 (four per warp) normally; a rank with so few
+// tokens that this would leave most SMs idle (fewer CTAs than half the SMs)
+// takes one token per warp, spreading its NVLink stores over more SMs.
 
 // Copies one row of H bf16 (H % 8 == 0) with the warp: up to 8 16-byte loads
 // per lane issued before their stores.
@@ -156,28 +158,29 @@ __device__ __forceinline__ void warp_copy_row(uint4 *__restrict__ dst, const uin
   }
 }
 
-// CTA = 32 consecutive tokens (warp w: tokens 4w..4w+3).  Pass 1 finds each
+// CTA = TPC consecutive tokens (TPC / 8 per warp).  Pass 1 finds each
 // token's owner ranks and its rank among this CTA's rows for each destination
 // (shared-memory counters); one global atomicAdd per destination then reserves
 // the CTA's block of rows in that destination's slab; pass 2 stores the rows.
 // x [T, H] bf16, idx/w [T, k]; ret_pos [T, N]: d*Tcap + t where rank d returns
 // token t's partial, else -1.
+template <int TPC>
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(
     const uint16_t *__restrict__ x, const int32_t *__restrict__ idx,
     const float *__restrict__ w, int64_t T, int k, int64_t H, int El, int N, int rank,
     int64_t Tcap, uint32_t *__restrict__ ctrl, const uint64_t *__restrict__ peers,
     DevLayout L, int32_t *__restrict__ ret_pos, const int32_t *__restrict__ owner, int *err) {
-  __shared__ uint32_t s_used[kTokPerCta];
-  __shared__ int32_t s_rank[kTokPerCta][kMaxRanks];
+  __shared__ uint32_t s_used[TPC];
+  __shared__ int32_t s_rank[TPC][kMaxRanks];
   __shared__ uint32_t s_cnt[kMaxRanks];
   __shared__ int32_t s_base[kMaxRanks];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * kTokPerCta;
+  const int64_t t0 = static_cast<int64_t>(blockIdx.x) * TPC;
   if (threadIdx.x < kMaxRanks) s_cnt[threadIdx.x] = 0u;
   __syncthreads();
   // ---- pass 1: owner ranks and local ranks
-  for (int i = 0; i < kTokPerCta / 8; ++i) {
-    const int tl = warp * (kTokPerCta / 8) + i;
+  for (int i = 0; i < TPC / 8; ++i) {
+    const int tl = warp * (TPC / 8) + i;
     const int64_t t = t0 + tl;
     uint32_t used = 0u;
     if (t < T) {
@@ -203,8 +206,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(
     s_base[threadIdx.x] = static_cast<int32_t>(atomicAdd(&ctrl[kCtrlSend + threadIdx.x], s_cnt[threadIdx.x]));
   __syncthreads();
   // ---- pass 2: rows, slot lists, weights and token ids into the owners' windows
-  for (int i = 0; i < kTokPerCta / 8; ++i) {
-    const int tl = warp * (kTokPerCta / 8) + i;
+  for (int i = 0; i < TPC / 8; ++i) {
+    const int tl = warp * (TPC / 8) + i;
     const int64_t t = t0 + tl;
     if (t >= T) break;
     int e = -1;
@@ -479,8 +482,10 @@ extern "C" int q35_ep_dispatch(const void *x, const int32_t *idx, const float *w
   const Layout L = window_layout(N, Tcap, H, k);
   uint8_t *win = static_cast<uint8_t *>(window);
   // at least one CTA: a rank with no tokens still publishes its (empty) counts
-  const int64_t ctas = T > 0 ? (T + kTokPerCta - 1) / kTokPerCta : 1;
-  ep_dispatch_kernel<<<static_cast<unsigned>(ctas), 256, 0,
+  const int tpc = (T + 31) / 32 < num_sms() / 2 ? 8 : 32;
+  const int64_t ctas = T > 0 ? (T + tpc - 1) / tpc : 1;
+  auto kern = tpc == 8 ? ep_dispatch_kernel<8> : ep_dispatch_kernel<32>;
+  kern<<<static_cast<unsigned>(ctas), 256, 0,
                        reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t *>(x), idx, w, T, k, H, El, N, rank, Tcap,
       reinterpret_cast<uint32_t *>(win + L.ctrl), reinterpret_cast<const uint64_t *>(win + L.peers),
