@@ -396,6 +396,7 @@ extern "C" int q35_embedding_fwd(const void *table, const int64_t *ids, void *ou
     return fail(Q35_ERR_SHAPE, "embedding: n %lld V %lld cols %lld (x8)", (long long)n,
                 (long long)V, (long long)cols);
   if (!aligned16(table) || !aligned16(out)) return fail(Q35_ERR_ALIGN, "embedding: alignment");
+  if ((n + 7) / 8 >= (int64_t(1) << 31)) return fail(Q35_ERR_SHAPE, "embedding: too many ids");
   if (n == 0) return Q35_OK;
   int *err = device_error_word();
   if (!err) return fail(Q35_ERR_CUDA, "embedding: no device error word");
